@@ -1,0 +1,372 @@
+"""Benchmark: WKV-7 slot decode on B200, RWKV-7 1.5B state shape.
+
+Workload (one "step" = one decode token for every active slot through all
+layers): L=24 layers, H=32 heads, head dim N=64, a 1024-slot fp32 arena
+(+ reserved slot 0, 12.9 GB), 256 active slots drawn without replacement by
+seeded int32 ids. Each layer is one wkv7_decode_slots launch that reads the
+256x32 head states from the arena, applies the RWKV-7 update and writes them
+back in place. Inputs are seeded synthetic activations with the op-level
+distributions of the reference configuration (no dataset exists for this
+path). The per-step state traffic (6.4 GB) exceeds the 126 MB L2, so no L2
+flush is needed between steps.
+
+  value  — device-timed tokens/s (inputs resident in HBM, CUDA graph of the
+           24 launches per step, CUDA events on the launching stream)
+  e2e    — tokens/s through the public op (ops.wkv7_decode_slots) with host
+           buffers: every step copies its r,w,k,v,kk,a for all layers and the
+           slot ids from pinned host memory and reads every layer's o back.
+  roofline — algorithmic bytes per launch / average launch time, vs the
+           measured HBM copy bandwidth.
+
+Multi-GPU: one process per GPU (torchrun), each GPU holds its own arena
+shard and 256 active slots; no collective on the data path (weak scaling).
+``--impl reference`` times the CPU restatement of the reference recurrence
+(oracle/, fp32, all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+L, H, N, NUM_SLOTS, ACTIVE = 24, 32, 64, 1024, 256
+BYTES_PER_HEAD = 2 * N * N * 4 + 6 * N * 2 + N * 2  # state r+w, 6 inputs, o = 33,664 B
+METRIC = "WKV-7 slot-decode tokens/s @1/2/4/8 B200; achieved HBM GB/s vs peak"
+PROFILE = ROOT / "profiles" / "wkv7_decode_slots_cfg1.txt"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch recorded from an ncu capture (profiles/)."""
+    if not PROFILE.exists():
+        return None
+    for line in PROFILE.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_inputs(dev, seed):
+    from wkvm_b200 import synth
+    per_layer = []
+    for layer in range(L):
+        x = synth.rwkv7_inputs(ACTIVE, 1, H, N, seed=seed * 1000 + layer, device=dev,
+                               state=False)
+        per_layer.append([x[n] for n in ("r", "w", "k", "v", "kk", "a")])
+    return per_layer
+
+
+def run_ours(args, world, rank, local):
+    from wkvm_b200 import ops, synth
+    from wkvm_b200.state import RWKV7StateBank, RWKV7StateLayout
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    layout = RWKV7StateLayout(n_layer=L, hidden_size=H * N, num_heads=H, head_dim=N,
+                              head_v_dim=N, dtype=torch.bfloat16)
+    bank = RWKV7StateBank(layout, NUM_SLOTS, device=dev)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    bank.wkv.normal_(0.0, 0.1, generator=g)
+    ids_host = synth.slot_ids(ACTIVE, NUM_SLOTS + 1, seed=rank)
+    ids = ops.slot_ids_tensor(ids_host, NUM_SLOTS + 1, dev)
+    inputs = make_inputs(dev, seed=rank)
+    outs = [torch.empty(ACTIVE, 1, H, N, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+    ops.status_word(dev)
+
+    def step():
+        for layer in range(L):
+            ops.wkv7_decode_slots(*inputs[layer], bank.wkv, layer, ids, out=outs[layer])
+
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index if dev.index is not None else 0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record()
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world, dev)
+    ops.check_device_status(dev)
+
+    # ---- end-to-end through the public op with host buffers ----
+    host_in = [[t.cpu().pin_memory() for t in layer_in] for layer_in in inputs]
+    host_out = [torch.empty_like(o, device="cpu").pin_memory() for o in outs]
+    dev_in = [[torch.empty_like(t) for t in layer_in] for layer_in in inputs]
+    ids_list = ids_host.tolist()
+    h2d = sum(t.numel() * t.element_size() for li in host_in for t in li) + 4 * ACTIVE
+    d2h = sum(o.numel() * o.element_size() for o in host_out)
+
+    def e2e_step():
+        dids = ops.slot_ids_tensor(ids_list, NUM_SLOTS + 1, dev)
+        for layer in range(L):
+            for d, hsrc in zip(dev_in[layer], host_in[layer]):
+                d.copy_(hsrc, non_blocking=True)
+            o = ops.wkv7_decode_slots(*dev_in[layer], bank.wkv, layer, dids)
+            host_out[layer].copy_(o, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e_steps = max(1, args.steps)
+    s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(e_steps):
+        e2e_step()
+    t2.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(s2.elapsed_time(t2), world, dev)
+    ops.check_device_status(dev)
+
+    if rank != 0:
+        return None
+    step_ms = ms / args.steps
+    launch_ms = step_ms / L
+    bytes_per_launch = ACTIVE * H * BYTES_PER_HEAD
+    achieved = bytes_per_launch / (launch_ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    tokens_per_s = world * ACTIVE * args.steps / (ms * 1e-3)
+    traffic = profiled_traffic()
+    line = {
+        "metric": METRIC,
+        "value": round(tokens_per_s, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 in/out, fp32 state",
+        "data": "synthetic (seeded, reference op-level distributions)",
+        "config": {
+            "workload": "RWKV-7 1.5B-shape WKV slot decode: L=24 H=32 N=64, 256 active of "
+                        "1024 arena slots per GPU, all layers per step",
+            "global_batch": ACTIVE * world,
+            "slots_per_gpu": NUM_SLOTS,
+            "parallelism": f"slot-sharded x{world}, no collective",
+            "graph": "CUDA graph of 24 per-layer launches",
+            "l2": "no flush: 6.4 GB state traffic per step > 126 MB L2",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "wkv7_recurrent_kernel<64,16,bf16,mul> (wkv7_decode_slots)",
+            "achieved": round(achieved, 1),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "peak_kind": f"{peak_kind} hbm_gbs",
+            "bytes_per_launch": bytes_per_launch,
+            "traffic": traffic,
+        },
+        "clocks": clk.summary(),
+        "gpu_launches": L * args.steps,
+        "e2e": {
+            "value": round(world * ACTIVE * e_steps / (e2e_ms * 1e-3), 1),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "path": "ops.wkv7_decode_slots with pinned-host inputs/outputs and host slot ids",
+        },
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_sample_slots)
+    return line
+
+
+def _cpu_sample(slots: int, threads: int, seed: int = 0):
+    """One decode token through all 24 layers for ``slots`` slots with the
+    fp32 oracle; returns seconds."""
+    from oracle import oracle
+    from wkvm_b200 import synth
+    import numpy as np
+    xs = []
+    for layer in range(L):
+        x = synth.rwkv7_inputs(slots, 1, H, N, seed=seed * 1000 + layer)
+        xs.append([x[n].float().numpy() for n in ("r", "w", "k", "v", "kk", "a")] +
+                  [x["h0"].numpy()])
+    t0 = time.perf_counter()
+    for r, w, k, v, kk, a, h0 in xs:
+        oracle.rwkv7_recurrence(r, w, k, v, kk, a, initial_state=h0, threads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(slots: int):
+    threads = os.cpu_count() or 1
+    reps, total = 0, 0.0
+    while total < 10.0 and reps < 50:
+        total += _cpu_sample(slots, threads, seed=reps)
+        reps += 1
+    return {"value": round(reps * slots / total, 2), "unit": "tokens/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{reps} x ({slots} slots x 24 layers x 32 heads, one token) through the "
+                      f"fp32 C oracle (oracle/wkv_oracle.c), {threads} threads"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    slots = args.cpu_sample_slots
+    for i in range(args.warmup):
+        _cpu_sample(slots, threads, seed=i)
+    times = [_cpu_sample(slots, threads, seed=100 + i) for i in range(args.steps)]
+    total = sum(times)
+    value = round(slots * args.steps / total, 2)
+    return {
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, reference op-level distributions)",
+        "config": {"workload": "RWKV-7 1.5B-shape WKV slot decode: L=24 H=32 N=64; each step a "
+                               f"bounded sample of {slots} of the 256 active slots",
+                   "global_batch": slots, "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{slots} slots x 24 layers x 32 heads per step, fp32 C "
+                                   "restatement of fla's recurrence (oracle/wkv_oracle.c)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-sample-slots", type=int, default=16)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+    else:
+        world, rank, local = dist_setup()
+        line = run_ours(args, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,197 @@
+/*
+ * wkvm_b200 — C ABI of the B200 (sm_100a) state-slot hot path of wkvm.
+ *
+ * The path: the RWKV-7 WKV recurrence (a diagonal-plus-low-rank "DPLR" delta
+ * rule) and its gated-delta-rule (GDN) sibling, over fixed-size fp32
+ * per-request state slots, plus the slot copies around it.
+ *
+ * Conventions shared by every entry point:
+ *   - all tensor pointers are device pointers (snapshot/restore also take a
+ *     pinned host pointer, named as such), row-major, contiguous;
+ *   - activations are [B, T, H, D] with element type `dtype` (WKVM_DTYPE_*);
+ *   - recurrent states are fp32 [.., H, K, V], element h[k][v] (k rows, v
+ *     contiguous), the layout of fla and of wkvm's RWKV7StateBank.wkv;
+ *   - a "slot bank layer" is the fp32 tensor bank.wkv[layer] of shape
+ *     [num_slots, H, K, V] where num_slots counts the reserved padding slot 0
+ *     (wkvm allocates S+1 rows for S usable slots);
+ *   - slot ids are int32 device arrays; ids must lie in [0, num_slots) and a
+ *     batch must not name one slot twice (the host wrapper checks this; the
+ *     kernels re-check the range and skip out-of-range rows, reporting
+ *     WKVM_ERR_SLOT_RANGE into `status`);
+ *   - `status` is an optional device int32 (may be NULL) that receives the
+ *     first device-side error; it is never cleared by the library;
+ *   - every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream) and returns 0 or a negative WKVM_ERR_* code for
+ *     argument errors found on the host before anything is launched.
+ *
+ * Reference citations use fla = flash-linear-attention 0.5.1 (the package
+ * wkvm's RWKV-7 model delegates its WKV arithmetic to) and wkvm = xiaol/wkvm.
+ */
+#ifndef WKVM_B200_H_
+#define WKVM_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* wkvm_stream_t; /* == cudaStream_t */
+
+enum {
+  WKVM_OK = 0,
+  WKVM_ERR_INVALID_ARG = -1,  /* null pointer, negative size, bad flag */
+  WKVM_ERR_SHAPE = -2,        /* head dim / shape not supported */
+  WKVM_ERR_DTYPE = -3,        /* dtype code not supported */
+  WKVM_ERR_SLOT_RANGE = -4,   /* slot id outside [0, num_slots) */
+  WKVM_ERR_DUPLICATE = -5,    /* one slot named twice in a batch */
+  WKVM_ERR_CUDA = -6,         /* a CUDA runtime call failed */
+  WKVM_ERR_ALIGN = -7,        /* pointer or row size not 16-byte aligned */
+  WKVM_ERR_UNSUPPORTED = -8,  /* option not implemented */
+  WKVM_ERR_TIMEOUT = -9       /* bounded wait ran out */
+};
+
+enum { WKVM_DTYPE_F32 = 0, WKVM_DTYPE_BF16 = 1, WKVM_DTYPE_F16 = 2 };
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int wkvm_version(void);
+
+/* Static text for a WKVM_ERR_* code. */
+const char* wkvm_strerror(int code);
+
+/* ------------------------------------------------------------------------
+ * RWKV-7 recurrent form (decode, and short prefill tails).
+ *
+ * Replaces fla `fused_mul_recurrent_rwkv7` (fla/ops/rwkv7/fused_recurrent.py:240,
+ * kernel :34-129, decode branch :88-102), called by fla's RWKV7Attention at
+ * fla/layers/rwkv7.py:323-334 with scale=1. Per token, per head:
+ *   sa[v] = sum_k (-kk[k]) h[k][v]            (pre-update state)
+ *   h[k][v] = exp(w[k]) h[k][v] + kk[k] a[k] sa[v] + k[k] v[v]
+ *   o[v]   = sum_k r[k] scale h[k][v]          (post-update state)
+ * w is the log-decay. `h0` (optional, [N,H,K,V]) is the initial state, `ht`
+ * (optional) receives the final state; h0 == ht is allowed (in-place).
+ * cu_seqlens (optional, int64 device [N+1]) selects varlen mode with B == 1.
+ * ------------------------------------------------------------------------ */
+int wkvm_fused_mul_recurrent_rwkv7(
+    const void* r, const void* w, const void* k, const void* v,
+    const void* kk, const void* a, void* o,
+    const float* h0, float* ht, const int64_t* cu_seqlens,
+    int32_t B, int32_t T, int32_t H, int32_t K, int32_t V,
+    float scale, int32_t dtype, int32_t* status, wkvm_stream_t stream);
+
+/* General DPLR recurrent form: replaces fla `fused_recurrent_rwkv7` /
+ * `fused_recurrent_dplr_delta_rule` (fla/ops/rwkv7/fused_recurrent.py:183,
+ * fla/ops/generalized_delta_rule/dplr/fused_recurrent.py) with explicit a, b:
+ *   h = exp(w) h + b (a^T h) + k v^T ;  o = h^T (r scale)                  */
+int wkvm_fused_recurrent_dplr(
+    const void* r, const void* w, const void* k, const void* v,
+    const void* a, const void* b, void* o,
+    const float* h0, float* ht, const int64_t* cu_seqlens,
+    int32_t B, int32_t T, int32_t H, int32_t K, int32_t V,
+    float scale, int32_t dtype, int32_t* status, wkvm_stream_t stream);
+
+/* Slot-native RWKV-7 decode: same arithmetic as
+ * wkvm_fused_mul_recurrent_rwkv7 (scale 1), but the state of batch row i is
+ * read from and written back to bank_layer[slot_ids[i]] in place. Replaces the
+ * gather -> fla kernel -> scatter sequence of wkvm RWKV7StateBank.gather_cache
+ * (wkvm/runner/state.py:63-83), fla fused_mul_recurrent_rwkv7 and
+ * RWKV7StateBank.scatter_cache (wkvm/runner/state.py:85-97) for one layer.
+ * T >= 1 tokens per row are applied in order (T > 1: fla's T-loop branch,
+ * fused_recurrent.py:103-125). Inputs [B,T,H,K]; o [B,T,H,V].             */
+int wkvm_wkv7_decode_slots(
+    const void* r, const void* w, const void* k, const void* v,
+    const void* kk, const void* a, void* o,
+    float* bank_layer, int64_t num_slots, const int32_t* slot_ids,
+    int32_t B, int32_t T, int32_t H, int32_t K, int32_t V,
+    int32_t dtype, int32_t* status, wkvm_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Gated delta rule (GDN) recurrent form.
+ *
+ * Replaces fla `fused_recurrent_gated_delta_rule`
+ * (fla/ops/gated_delta_rule/fused_recurrent.py:291, kernel :28-170) for
+ * head-wise g and beta, standard [K,V] state layout:
+ *   h = exp(g) h ; v' = beta (v - h^T k) ; h += k v'^T ; o = h^T (q scale)
+ * q, k: [B,T,H,K]; v, o: [B,T,HV,V]; g, beta: [B,T,HV]; HV % H == 0 (grouped
+ * value heads). use_qk_l2norm != 0 normalises q and k per head in-kernel as
+ * fla does (x / sqrt(sum x^2 + 1e-6)).                                    */
+int wkvm_fused_recurrent_gated_delta_rule(
+    const void* q, const void* k, const void* v, const void* g,
+    const void* beta, void* o,
+    const float* h0, float* ht, const int64_t* cu_seqlens,
+    int32_t B, int32_t T, int32_t H, int32_t HV, int32_t K, int32_t V,
+    float scale, int32_t use_qk_l2norm, int32_t dtype,
+    int32_t* status, wkvm_stream_t stream);
+
+/* Slot-native GDN decode: state of row i lives at bank_layer[slot_ids[i]]
+ * ([num_slots, HV, K, V] fp32) and is updated in place.                   */
+int wkvm_gdn_decode_slots(
+    const void* q, const void* k, const void* v, const void* g,
+    const void* beta, void* o,
+    float* bank_layer, int64_t num_slots, const int32_t* slot_ids,
+    int32_t B, int32_t T, int32_t H, int32_t HV, int32_t K, int32_t V,
+    float scale, int32_t use_qk_l2norm, int32_t dtype,
+    int32_t* status, wkvm_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Slot copies. A state family tensor is viewed as [outer, num_slots, row]:
+ * bank.wkv [L, S+1, H*K*V fp32] has outer = L; bank.shift [L, 2, S+1, D]
+ * has outer = 2L. `outer_stride` and `slot_stride` are in bytes, `row_bytes`
+ * is the bytes of one slot's row within one outer index. Copies are bitwise.
+ * Row bytes, strides and base pointers must be 16-byte aligned.
+ * ------------------------------------------------------------------------ */
+
+/* Fork: rows of dst_ids[i] <- rows of src_ids[i] (all outer indices).
+ * Defines on device what wkvm StateArena.fork leaves to the runner
+ * (wkvm/core/arena.py:82-92). src and dst sets must not overlap. */
+int wkvm_slot_copy(void* base, int64_t outer, int64_t outer_stride,
+                   int64_t slot_stride, int64_t row_bytes, int64_t num_slots,
+                   const int32_t* src_ids, const int32_t* dst_ids, int32_t n,
+                   int32_t* status, wkvm_stream_t stream);
+
+/* Zero the rows of ids[i]: wkvm RWKV7StateBank.zero_slots
+ * (wkvm/runner/state.py:50-54). */
+int wkvm_slot_zero(void* base, int64_t outer, int64_t outer_stride,
+                   int64_t slot_stride, int64_t row_bytes, int64_t num_slots,
+                   const int32_t* ids, int32_t n,
+                   int32_t* status, wkvm_stream_t stream);
+
+/* Snapshot: packed[i][o][:] <- base[o][ids[i]][:] for n slots into a packed
+ * buffer [n, outer, row_bytes] that may be pinned, device-mapped host memory
+ * (the layout of wkvm StateStore.save's bank.wkv[:, slot] host copy,
+ * wkvm/store.py:130-131,248-252). */
+int wkvm_slot_snapshot(const void* base, int64_t outer, int64_t outer_stride,
+                       int64_t slot_stride, int64_t row_bytes,
+                       int64_t num_slots, const int32_t* ids, int32_t n,
+                       void* packed, int32_t* status, wkvm_stream_t stream);
+
+/* Restore: base[o][ids[i]][:] <- packed[i][o][:] (wkvm StateStore.load,
+ * wkvm/store.py:151-153). */
+int wkvm_slot_restore(void* base, int64_t outer, int64_t outer_stride,
+                      int64_t slot_stride, int64_t row_bytes,
+                      int64_t num_slots, const int32_t* ids, int32_t n,
+                      const void* packed, int32_t* status,
+                      wkvm_stream_t stream);
+
+/* Live migration: rows of dst_ids[i] in dst_base (a peer GPU's bank, peer
+ * access enabled by the caller) <- rows of src_ids[i] in src_base. Both
+ * banks share outer/strides/row size. Plain peer stores over NVLink; launch
+ * on the source GPU's stream. No counterpart in the reference, whose README
+ * only plans it. */
+int wkvm_slot_migrate(const void* src_base, void* dst_base, int64_t outer,
+                      int64_t outer_stride, int64_t slot_stride,
+                      int64_t row_bytes, int64_t src_num_slots,
+                      int64_t dst_num_slots, const int32_t* src_ids,
+                      const int32_t* dst_ids, int32_t n, int32_t* status,
+                      wkvm_stream_t stream);
+
+/* Enables `device` -> `peer` access (cudaDeviceEnablePeerAccess with
+ * `device` current); already-enabled counts as success. Needed once per pair
+ * before wkvm_slot_migrate writes into the peer's bank. */
+int wkvm_enable_peer_access(int32_t device, int32_t peer);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WKVM_B200_H_ */
