@@ -185,6 +185,12 @@ int wkvm_slot_migrate(const void* src_base, void* dst_base, int64_t outer,
                       const int32_t* dst_ids, int32_t n, int32_t* status,
                       wkvm_stream_t stream);
 
+/* Self-test of the tensor-core layer the prefill kernels use: one tile
+ * D[128,N] = A[128,64] B[N,64]^T with tcgen05.mma kind::tf32, fp32 row-major
+ * device buffers, N in {64, 128}. No counterpart in the reference. */
+int wkvm_selftest_tf32_mma(const float* A, const float* B, float* D, int32_t N,
+                           int32_t* status, wkvm_stream_t stream);
+
 /* Enables `device` -> `peer` access (cudaDeviceEnablePeerAccess with
  * `device` current); already-enabled counts as success. Needed once per pair
  * before wkvm_slot_migrate writes into the peer's bank. */
