@@ -134,6 +134,41 @@ int wkvm_gdn_decode_slots(
     int32_t* status, wkvm_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Chunked prefill (WY / UT-transform form, 64-token chunks, tcgen05 tf32
+ * tensor cores, fp32 accumulation). Same arithmetic as the recurrent forms
+ * above, reassociated by chunk.
+ *
+ * Replaces fla `chunk_rwkv7` (fla/ops/rwkv7/chunk.py:13) ->
+ * `chunk_dplr_delta_rule` (fla/ops/generalized_delta_rule/dplr/chunk.py:442,
+ * forward :33-135), called by fla's RWKV7Attention for seq_len >= 64
+ * (fla/layers/rwkv7.py:305-321) with a = -kk, b = kk * a_gate, scale 1.
+ * K == V == 64 runs the tensor-core kernel; other head sizes run the
+ * recurrent kernel. The chunk kernel requires |sum of w| over any 32
+ * consecutive tokens <= 80 (RWKV-7's w = -0.6065 sigmoid(.) keeps it under
+ * 20) and reports WKVM_ERR_UNSUPPORTED in `status` otherwise.
+ * ------------------------------------------------------------------------ */
+int wkvm_chunk_dplr(
+    const void* r, const void* w, const void* k, const void* v,
+    const void* a, const void* b, void* o,
+    const float* h0, float* ht, const int64_t* cu_seqlens,
+    int32_t B, int32_t T, int32_t H, int32_t K, int32_t V,
+    float scale, int32_t dtype, int32_t* status, wkvm_stream_t stream);
+
+/* Slot-native RWKV-7 prefill: the initial state of sequence i is read from
+ * bank_layer[slot_ids[i]] and the final state written back there. Replaces
+ * wkvm RWKV7Runner.prefill's gather -> chunk_rwkv7 -> scatter round trip
+ * per host chunk (wkvm/runner/runner.py:52-62). Inputs (r, w, k, v, kk,
+ * a_gate) as for wkvm_wkv7_decode_slots; cu_seqlens (optional) packs
+ * variable-length sequences with B = number of sequences.                 */
+int wkvm_wkv7_prefill_slots(
+    const void* r, const void* w, const void* k, const void* v,
+    const void* kk, const void* a, void* o,
+    float* bank_layer, int64_t num_slots, const int32_t* slot_ids,
+    const int64_t* cu_seqlens,
+    int32_t B, int32_t T, int32_t H, int32_t K, int32_t V,
+    int32_t dtype, int32_t* status, wkvm_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Slot copies. A state family tensor is viewed as [outer, num_slots, row]:
  * bank.wkv [L, S+1, H*K*V fp32] has outer = L; bank.shift [L, 2, S+1, D]
  * has outer = 2L. `outer_stride` and `slot_stride` are in bytes, `row_bytes`

@@ -1,8 +1,11 @@
 """Prefill entry points (chunk_rwkv7 / chunk_gated_delta_rule and their
 slot-native forms).
 
-Sequences are run through the sm_100a kernels of libwkvm_b200.so; the
-initial state comes from ``initial_state`` (or a bank slot) and the final
+RWKV-7 (head dim 64) runs the fused chunked tensor-core kernel
+(wkvm_chunk_dplr / wkvm_wkv7_prefill_slots: tcgen05 tf32, 64-token chunks,
+state kept on chip across chunks). Other head sizes and the GDN sibling run
+the recurrent kernel, which streams the state once and loops over tokens.
+The initial state comes from ``initial_state`` (or a bank slot) and the final
 state goes to a new tensor (or back into the slot).
 """
 
@@ -15,8 +18,9 @@ from . import ops as _ops
 
 
 def chunk_dplr(r, w, k, v, a, b, scale, initial_state, output_final_state, cu_seqlens):
-    return _ops._rwkv7_recurrent("wkvm_fused_recurrent_dplr", r, w, k, v, a, b, scale,
-                                 initial_state, output_final_state, cu_seqlens)
+    """fla chunk_dplr_delta_rule semantics; returns (o, final_state or None)."""
+    return _ops._rwkv7_recurrent("wkvm_chunk_dplr", r, w, k, v, a, b, scale, initial_state,
+                                 output_final_state, cu_seqlens)
 
 
 def chunk_gdn(q, k, v, g, beta, scale, initial_state, output_final_state, use_qk_l2norm,
@@ -27,19 +31,35 @@ def chunk_gdn(q, k, v, g, beta, scale, initial_state, output_final_state, use_qk
         cu_seqlens=cu_seqlens)
 
 
-def wkv7_prefill_slots(r, w, k, v, kk, a, bank_wkv, layer, slot_ids, cu_seqlens=None):
-    if cu_seqlens is not None:
-        raise NotImplementedError("varlen slot prefill: pass one row per sequence")
-    return _ops.wkv7_decode_slots(r, w, k, v, kk, a, bank_wkv, layer, slot_ids)
+def wkv7_prefill_slots(r, w, k, v, kk, a, bank_wkv, layer, slot_ids, cu_seqlens=None,
+                       out=None):
+    """RWKV-7 prefill with initial and final state in bank_wkv[layer, slot_ids].
+    Inputs [B, T, H, N] (or [1, total, H, N] with cu_seqlens); returns o."""
+    _ops._require_cuda(r, w, k, v, kk, a, bank_wkv)
+    layer_t = _ops._bank_layer(bank_wkv, layer)
+    (r, w, k, v, kk, a), dt = _ops._acts(r, w, k, v, kk, a)
+    B, T, H, K = r.shape
+    V = v.shape[-1]
+    if tuple(layer_t.shape[1:]) != (H, K, V):
+        raise ValueError("bank layer shape does not match H, K, V")
+    _ops._check_varlen(r, None, cu_seqlens)
+    nseq = B if cu_seqlens is None else len(cu_seqlens) - 1
+    ids = _ops.slot_ids_tensor(slot_ids, layer_t.shape[0], r.device)
+    if ids.numel() != nseq:
+        raise ValueError(f"{ids.numel()} slot ids for {nseq} sequences")
+    cu = _ops._cu(cu_seqlens, r.device)
+    o = torch.empty_like(v) if out is None else out
+    with torch.cuda.device(r.device):
+        _lib.call("wkvm_wkv7_prefill_slots", _ops._ptr(r), _ops._ptr(w), _ops._ptr(k),
+                  _ops._ptr(v), _ops._ptr(kk), _ops._ptr(a), _ops._ptr(o), _ops._ptr(layer_t),
+                  layer_t.shape[0], _ops._ptr(ids), _ops._ptr(cu), nseq, T, H, K, V, dt,
+                  _ops._ptr(_ops.status_word(r.device)), _ops._stream(r.device))
+    return o
 
 
 def gdn_prefill_slots(q, k, v, g, beta, bank, layer, slot_ids, scale, use_qk_l2norm,
                       cu_seqlens=None):
     if cu_seqlens is not None:
-        raise NotImplementedError("varlen slot prefill: pass one row per sequence")
+        raise NotImplementedError("varlen GDN slot prefill: pass one row per sequence")
     return _ops.gdn_decode_slots(q, k, v, g, beta, bank, layer, slot_ids, scale,
                                  use_qk_l2norm)
-
-
-__all__ = ["chunk_dplr", "chunk_gdn", "wkv7_prefill_slots", "gdn_prefill_slots"]
-_ = (_lib, torch)
