@@ -222,9 +222,10 @@ int wkvm_slot_migrate(const void* src_base, void* dst_base, int64_t outer,
 
 /* Self-test of the tensor-core layer the prefill kernels use: one tile
  * D[128,N] = A[128,64] B[N,64]^T with tcgen05.mma kind::tf32, fp32 row-major
- * device buffers, N in {64, 128}. No counterpart in the reference. */
+ * device buffers, N in {64, 128}; a_in_tmem != 0 feeds A from tensor
+ * memory instead of shared memory. No counterpart in the reference. */
 int wkvm_selftest_tf32_mma(const float* A, const float* B, float* D, int32_t N,
-                           int32_t* status, wkvm_stream_t stream);
+                           int32_t a_in_tmem, int32_t* status, wkvm_stream_t stream);
 
 /* Enables `device` -> `peer` access (cudaDeviceEnablePeerAccess with
  * `device` current); already-enabled counts as success. Needed once per pair

@@ -14,12 +14,13 @@ def _tf32(x):
 
 
 @pytest.mark.parametrize("N", [64, 128])
-def test_tf32_tile_matches_fp64(cuda, N):
+@pytest.mark.parametrize("a_in_tmem", [0, 1])
+def test_tf32_tile_matches_fp64(cuda, N, a_in_tmem):
     g = torch.Generator().manual_seed(N)
     A = _tf32(torch.randn(128, 64, generator=g)).to(cuda)
     B = _tf32(torch.randn(N, 64, generator=g)).to(cuda)
     D = torch.full((128, N), float("nan"), device=cuda)
-    _lib.call("wkvm_selftest_tf32_mma", A.data_ptr(), B.data_ptr(), D.data_ptr(), N,
+    _lib.call("wkvm_selftest_tf32_mma", A.data_ptr(), B.data_ptr(), D.data_ptr(), N, a_in_tmem,
               ops.status_word(cuda).data_ptr(), torch.cuda.current_stream().cuda_stream)
     ops.check_device_status(cuda)
     ref = (A.double() @ B.double().T)

@@ -2,22 +2,28 @@
 // sm_100a tensor core (tcgen05.mma kind::tf32, fp32 accumulators in TMEM).
 //
 // One CTA owns one (sequence, head) and walks its 64-token chunks in order,
-// keeping every intermediate in shared memory and TMEM; HBM sees only the
-// bf16 inputs, the bf16 outputs and the fp32 state once in and once out.
+// keeping every intermediate on chip; HBM sees only the 16-bit inputs, the
+// 16-bit outputs and the fp32 state once in and once out.
 //
 // Per chunk (rows t, s = tokens, k, j = key index, v = value index; G = the
 // inclusive cumulative log-decay, Gx = G - w the exclusive one, g0 = G at the
 // chunk midpoint as a scaling reference, C = the last row):
 //   [a e^(Gx-g0); r e^(G-g0)] x [k e^(g0-G); b e^(g0-G)]^T
 //        -> A_ak (s<t), A_ab (s<t), A_qk (s<=t), A_qb (s<=t)         (MMA 1)
-//   A_ak V                                                            (MMA 2)
+//   [A_ak; A_qk] x V          (top half = A_ak V)                     (MMA 2)
 //   (I - A_ab) [W | U~] = [a e^Gx | A_ak V]     forward substitution, fp32
-//   [A_qb; Bh^T] x [W | U~] + [A_qk; Kh^T] x V                       (MMA 3)
+//   [Bh^T; A_qb] x W                                                  (MMA 3a)
+//   [Bh^T; A_qb] x U~ + [Kh^T; A_qk] x V = [N; O_intra]               (MMA 3b)
 //        with Kh = k e^(G_C - G), Bh = b e^(G_C - G)
-//   P = r e^G + A_qb W,  M = diag(e^G_C) + Bh^T W
-//   [O; S'] = [P; M] x S + [A_qk V + A_qb U~; Kh^T V + Bh^T U~]       (MMA 4)
-// MMA 4 accumulates onto the TMEM columns MMA 3 left, so the chunk's
-// output and next state come out of one instruction group.
+//   M = diag(e^G_C) + Bh^T W,  P = r e^G + A_qb W
+//   [S'; O] = [M; P] x S + [N; O_intra]                               (MMA 4)
+//
+// Every A operand lives in tensor memory: MMA 1's accumulator is masked in
+// place and fed back as the A operand of MMAs 2 and 3, whose accumulators in
+// turn become MMA 4's A operand, so only B operands go through shared memory.
+// TMEM: [0,64) a~/r~ -> A_ak V -> [M; P]; [64,192) MMA 1's result, later
+// [Kh^T | Bh^T] in its upper lanes; [192,256) [N; O_intra] -> [S'; O];
+// [256,320) r e^G for the output rows.
 //
 // Algebra and operand orientation are this file's own; the chunk recurrence
 // is the one fla's chunk_dplr_delta_rule implements
@@ -31,23 +37,38 @@ namespace {
 
 constexpr int CH = 64;             // chunk length
 constexpr int HD = 64;             // head dim (K == V)
-constexpr int NTHREADS = 128;      // one thread per TMEM lane
+constexpr int NTHREADS = 256;      // two warps per TMEM lane quarter
+constexpr int NIN = 6;             // r, w, k, v, x5, x6 input streams
 constexpr uint32_t LBO = 128;      // K-adjacent core matrices
 constexpr uint32_t SBO = 2048;     // 8-row groups of a 64-wide K tile
-constexpr uint32_t TILE = 16384;   // 64 x 64 fp32
+constexpr uint32_t LBO_S = 144;    // S^T: padded so column writes hit distinct banks
+constexpr uint32_t SBO_S = 16 * LBO_S;
 constexpr uint32_t KSTEP = 2 * LBO;  // 8 tf32 (32 bytes) of K per MMA
-// shared-memory regions (bytes), reused across a chunk as noted
-constexpr uint32_t R1 = 0;               // [a~; r~] -> {A_ab, A_ak V} row-major -> [P; M]
-constexpr uint32_t R2 = R1 + 2 * TILE;   // [k~; b~] -> [W^T; U~^T]
-constexpr uint32_t R3 = R2 + 2 * TILE;   // G scratch | [A_ak][A_qk][Kh^T]
-constexpr uint32_t R4 = R3 + 3 * TILE;   // [A_qb][Bh^T]
-constexpr uint32_t R5 = R4 + 2 * TILE;   // V^T
-constexpr uint32_t R6 = R5 + TILE;       // S^T (the running state)
-constexpr uint32_t R7 = R6 + TILE;       // a e^Gx row-major
-constexpr uint32_t R8 = R7 + TILE;       // r e^G row-major
-constexpr uint32_t SMEM_USED = R8 + TILE;
-constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;  // + alignment slack
-constexpr uint32_t TMEM_COLS = 256;
+constexpr int RS = 68;             // row stride (floats) of row-major scratch
+constexpr int STG_ROW = 144;       // bytes per staged 64 x 16-bit input row (+16 pad)
+
+// shared-memory regions (bytes)
+constexpr uint32_t S_STG = 0;                                   // raw inputs [6][64 rows]
+constexpr uint32_t S_G = S_STG + NIN * CH * STG_ROW;            // G row-major (stride RS)
+constexpr uint32_t S_AKV = S_G + CH * RS * 4;                   // A_ak V row-major
+constexpr uint32_t S_AAB = S_AKV + CH * RS * 4;                 // A_ab row-major
+constexpr uint32_t S_AG = S_AAB + CH * RS * 4;                  // a e^Gx row-major
+constexpr uint32_t S_RB = S_AG + CH * RS * 4;                   // [k~; b~] -> [W^T; U~^T]
+constexpr uint32_t S_VT = S_RB + 2 * 8 * SBO;                   // V^T
+constexpr uint32_t S_ST = S_VT + 8 * SBO;                       // S^T (the running state)
+constexpr uint32_t SMEM_USED = S_ST + 8 * SBO_S;
+constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;               // + alignment slack
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+
+// The shared-memory footprint allows one CTA per SM, so the CTA takes all
+// 512 TMEM columns.
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t T_A1 = 0;     // a~/r~, then A_ak V, then [M; P]
+constexpr uint32_t T_D1 = 64;    // MMA 1 accumulator (128 columns)
+constexpr uint32_t T_D3 = 192;   // [N; O_intra] -> [S'; O]
+constexpr uint32_t T_RG = 256;   // r e^G, rows in lanes 64..127
+
+enum { IN_R = 0, IN_W, IN_K, IN_V, IN_5, IN_6 };
 
 struct ChunkArgs {
   const void *p0, *p1, *p2, *p3, *p4, *p5;  // r, w, k, v, (kk | a), (a_gate | b)
@@ -62,31 +83,42 @@ struct ChunkArgs {
   int* status;
 };
 
-__device__ __forceinline__ void kst(uint8_t* tile, int row, int k, float x) {
-  *reinterpret_cast<float*>(tile + tc::kmajor_off(row, k, LBO, SBO)) = x;
-}
 __device__ __forceinline__ void kst4(uint8_t* tile, int row, int k, float4 x) {
   *reinterpret_cast<float4*>(tile + tc::kmajor_off(row, k, LBO, SBO)) = x;
+}
+__device__ __forceinline__ void st4(float* p, const float* x) {
+  *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ float stg(const uint8_t* sm, int in, int t, int k) {
+  return to_f32(reinterpret_cast<const T*>(sm + S_STG + (in * CH + t) * STG_ROW)[k]);
+}
+
+// 8 consecutive 16-bit inputs of row t starting at column k (k % 8 == 0).
+template <typename T>
+__device__ __forceinline__ void stg8(const uint8_t* sm, int in, int t, int k, float (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(sm + S_STG + (in * CH + t) * STG_ROW + k * 2);
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = to_f32(e[i]);
 }
 
 template <typename T>
 __device__ __forceinline__ void store_row32(T* dst, const float (&v)[32]) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) dst[i] = from_f32<T>(v[i]);
-}
-template <>
-__device__ __forceinline__ void store_row32<__nv_bfloat16>(__nv_bfloat16* dst, const float (&v)[32]) {
-#pragma unroll
   for (int i = 0; i < 32; i += 8) {
     uint4 u;
-    __nv_bfloat162 b0 = __floats2bfloat162_rn(v[i + 0], v[i + 1]);
-    __nv_bfloat162 b1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
-    __nv_bfloat162 b2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
-    __nv_bfloat162 b3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
-    u.x = *reinterpret_cast<uint32_t*>(&b0);
-    u.y = *reinterpret_cast<uint32_t*>(&b1);
-    u.z = *reinterpret_cast<uint32_t*>(&b2);
-    u.w = *reinterpret_cast<uint32_t*>(&b3);
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) e[j] = from_f32<T>(v[i + j]);
     *reinterpret_cast<uint4*>(dst + i) = u;
   }
 }
@@ -98,6 +130,18 @@ __device__ __forceinline__ void sync_tc() {
   tc::fence_after_sync();
 }
 
+// b from the two extra input streams (MUL: kk, a_gate -> b = kk * a_gate in
+// fp32 as fla's fused_mul_recurrent_rwkv7 does; otherwise b itself).
+template <typename T, bool MUL>
+__device__ __forceinline__ float in_b(const uint8_t* sm, int t, int k) {
+  const float x6 = stg<T>(sm, IN_6, t, k);
+  return MUL ? stg<T>(sm, IN_5, t, k) * x6 : x6;
+}
+
+// Thread roles: warp w serves TMEM lane quarter (w & 3); the two warps of a
+// quarter split the 64 columns of each row into halves g = w >> 2. A thread's
+// accumulator row is l = 32 (w & 3) + lane; rows 0..63 ("lo") carry the
+// a/k-side and state rows, rows 64..127 the r/b-side and output rows.
 template <typename Tin, bool MUL>
 __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
   extern __shared__ uint8_t smem_raw[];
@@ -105,13 +149,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
                                            ~static_cast<uintptr_t>(1023));
   __shared__ uint64_t mbar;
   __shared__ uint32_t tmem_slot;
-  __shared__ float s_gc[HD];
+  __shared__ float s_gc[HD];    // e^{G_C}
+  __shared__ float s_ref[HD];   // G at the chunk midpoint
+  __shared__ float s_eref[HD];  // e^{G at the midpoint}
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nh = blockIdx.x;
-  const int n = nh / p.H;
-  const int hh = nh - n * p.H;
+  const int quarter = warp & 3;
+  const int g = warp >> 2;                 // column half
+  const int l = quarter * 32 + lane;       // accumulator row / TMEM lane
+  const bool lo = l < 64;
+  const int r64 = l & 63;
+  const int c0 = g * 32;                   // first column of this thread's half
   const int H = p.H;
+  const int n = blockIdx.x / H;
+  const int hh = blockIdx.x - n * H;
 
   int64_t row = n;
   if (p.ids) {
@@ -131,265 +182,340 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     bos = (int64_t)n * p.T;
     len = p.T;
   }
-  const Tin* __restrict__ gr = static_cast<const Tin*>(p.p0);
-  const Tin* __restrict__ gw = static_cast<const Tin*>(p.p1);
-  const Tin* __restrict__ gk = static_cast<const Tin*>(p.p2);
-  const Tin* __restrict__ gv = static_cast<const Tin*>(p.p3);
-  const Tin* __restrict__ g5 = static_cast<const Tin*>(p.p4);
-  const Tin* __restrict__ g6 = static_cast<const Tin*>(p.p5);
+  const char* gin[NIN] = {static_cast<const char*>(p.p0), static_cast<const char*>(p.p1),
+                          static_cast<const char*>(p.p2), static_cast<const char*>(p.p3),
+                          static_cast<const char*>(p.p4), static_cast<const char*>(p.p5)};
   Tin* __restrict__ go = static_cast<Tin*>(p.o);
+  float* Grow = reinterpret_cast<float*>(sm + S_G);
+  float* AkV = reinterpret_cast<float*>(sm + S_AKV);
+  float* Aab = reinterpret_cast<float*>(sm + S_AAB);
+  float* AG = reinterpret_cast<float*>(sm + S_AG);
 
   if (warp == 0) {
     tc::tmem_alloc(&tmem_slot, TMEM_COLS);
     tc::tmem_relinquish();
   }
   if (tid == 0) tc::mbar_init(&mbar, 1);
-  // S^T[v][k] = h[k][v]
+  // S^T[v][k] = h[k][v]; thread k = tid & 63 writes a quarter of column k
   for (int e = tid; e < HD * HD; e += NTHREADS) {
-    const int k = e >> 6, v = e & 63;
-    kst(sm + R6, v, k, p.h_in ? p.h_in[hoff + e] : 0.f);
+    const int k = e & 63, v = e >> 6;
+    const float x = p.h_in ? p.h_in[hoff + k * HD + v] : 0.f;
+    *reinterpret_cast<float*>(sm + S_ST + tc::kmajor_off(v, k, LBO_S, SBO_S)) = x;
   }
   sync_tc();
   const uint32_t tm = tmem_slot;
+  const uint32_t tq = tc::tmem_addr(tm, quarter * 32, 0);  // this warp's lane quarter
   uint32_t phase = 0;
   bool failed = false;
   const int nchunks = (int)((len + CH - 1) / CH);
-  float* G = reinterpret_cast<float*>(sm + R3);
-  float* Arow = reinterpret_cast<float*>(sm + R1);
-  float* AkV = reinterpret_cast<float*>(sm + R1 + TILE);
-  float* ag = reinterpret_cast<float*>(sm + R7);
-  float* rg = reinterpret_cast<float*>(sm + R8);
-  const int drow = warp * 32 + lane;  // TMEM lane == accumulator row of this thread
 
   auto wait_mma = [&]() -> bool {
-    bool ok = tc::mbar_wait(&mbar, phase);
+    const bool ok = tc::mbar_wait(&mbar, phase);
     phase ^= 1u;
     const bool any_bad = __syncthreads_or(!ok);
     tc::fence_after_sync();
     if (any_bad && tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
     return !any_bad;
   };
+  const uint32_t idesc64 = tc::idesc_tf32(128, 64);
+  const uint32_t idesc128 = tc::idesc_tf32(128, 128);
 
-  for (int c = 0; c < nchunks && !failed; ++c) {
+  for (int c = 0; c < nchunks; ++c) {
     const int64_t tok0 = bos + (int64_t)c * CH;
     const int64_t rem = len - (int64_t)c * CH;
     const int clen = rem < CH ? (int)rem : CH;
     const bool last = (c == nchunks - 1);
 
-    // ---- cumulative log-decay G[t][k] (two halves of 32 tokens, then joined)
+    // ---- stage the chunk's raw inputs (one batch of 16-byte async copies)
     {
-      const int k = tid & 63, half = tid >> 6;
-      float g = 0.f;
-      for (int i = 0; i < 32; ++i) {
-        const int t = half * 32 + i;
-        const float wt = (t < clen) ? to_f32(gw[((tok0 + t) * H + hh) * HD + k]) : 0.f;
-        g += wt;
-        G[t * 64 + k] = g;
-      }
-    }
-    __syncthreads();
-    if (tid >= 64) {
-      const int k = tid - 64;
-      const float base = G[31 * 64 + k];
-      for (int t = 32; t < 64; ++t) G[t * 64 + k] += base;
-    }
-    __syncthreads();
-
-    // ---- elementwise operands
-    if (tid < 64) {
-      s_gc[tid] = expf(G[63 * 64 + tid]);
-      // exp(+-(G - G_mid)) must stay finite in fp32 (e^88); RWKV-7's decay
-      // (w >= -0.61 per token) keeps the span under 20.
-      const float span = fmaxf(fabsf(G[tid] - G[31 * 64 + tid]), fabsf(G[63 * 64 + tid] - G[31 * 64 + tid]));
-      if (span > 80.f) report(p.status, WKVM_ERR_UNSUPPORTED);
-    }
-#pragma unroll 2
-    for (int i = 0; i < (CH * HD) / NTHREADS; ++i) {
-      const int e = i * NTHREADS + tid;
-      const int t = e >> 6, k = e & 63;
-      float rr = 0.f, wt = 0.f, kv = 0.f, vv = 0.f, aa = 0.f, bb = 0.f;
-      if (t < clen) {
-        const int64_t gi = ((tok0 + t) * H + hh) * HD + k;
-        rr = to_f32(gr[gi]) * p.scale;
-        wt = to_f32(gw[gi]);
-        kv = to_f32(gk[gi]);
-        vv = to_f32(gv[gi]);
-        const float x5 = to_f32(g5[gi]);
-        const float x6 = to_f32(g6[gi]);
-        aa = MUL ? -x5 : x5;
-        bb = MUL ? x5 * x6 : x6;
-      }
-      const float gt = G[t * 64 + k];
-      const float gx = gt - wt;
-      const float ref = G[31 * 64 + k];
-      const float gc = G[63 * 64 + k];
-      kst(sm + R1, t, k, aa * expf(gx - ref));
-      kst(sm + R1, 64 + t, k, rr * expf(gt - ref));
-      const float einv = expf(ref - gt);
-      kst(sm + R2, t, k, kv * einv);
-      kst(sm + R2, 64 + t, k, bb * einv);
-      ag[t * 64 + k] = aa * expf(gx);
-      rg[t * 64 + k] = rr * expf(gt);
-      const float ec = expf(gc - gt);
-      kst(sm + R3 + 2 * TILE, k, t, kv * ec);  // Kh^T
-      kst(sm + R4 + TILE, k, t, bb * ec);      // Bh^T
-      kst(sm + R5, k, t, vv);                  // V^T
-    }
-    sync_tc();
-
-    // ---- MMA 1: [a~; r~] x [k~; b~]^T -> TMEM cols [0, 128)
-    if (tid == 0) {
-      const uint32_t id = tc::idesc_tf32(128, 128);
-      const uint32_t a0 = tc::smem_u32(sm + R1), b0 = tc::smem_u32(sm + R2);
-      for (int kk = 0; kk < HD / 8; ++kk)
-        tc::mma_tf32(tm, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO),
-                     tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), id, kk > 0);
-      tc::mma_commit(&mbar);
-    }
-    if (!wait_mma()) { failed = true; break; }
-
-    // ---- split into the four masked intra-chunk matrices
-#pragma unroll 1
-    for (int cb = 0; cb < 4; ++cb) {
-      float vals[32];
-      tc::tmem_ld32(tc::tmem_addr(tm, warp * 32, cb * 32), vals);
-      const bool kcols = cb < 2;
-      if (drow < 64) {
-        const int t = drow;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int s = (cb & 1) * 32 + i;
-          const float x = (s < t) ? vals[i] : 0.f;
-          if (kcols) kst(sm + R3, t, s, x);   // A_ak
-          else Arow[t * 64 + s] = x;          // A_ab (row-major, for the solve)
+      const uint32_t base = tc::smem_u32(sm + S_STG);
+      constexpr int PIECES = NIN * CH * (HD * 2 / 16);  // 16-byte pieces
+#pragma unroll 4
+      for (int e = tid; e < PIECES; e += NTHREADS) {
+        const int in = e / (CH * 8);
+        const int t = (e / 8) % CH;
+        const int piece = e % 8;
+        const uint32_t off = (in * CH + t) * STG_ROW + piece * 16;
+        if (t < clen) {
+          cp_async16(base + off, gin[in] + (((tok0 + t) * H + hh) * HD) * 2 + piece * 16);
+        } else {
+          *reinterpret_cast<uint4*>(sm + S_STG + off) = make_uint4(0, 0, 0, 0);
         }
+      }
+      cp_async_wait_all();
+      __syncthreads();
+    }
+
+    // ---- E1: threads 0..127 scan half a column of w each; 128..255 write V^T
+    if (tid < 128) {
+      const int k = tid & 63, t0 = (tid >> 6) * 32;
+      float acc = 0.f;
+#pragma unroll 8
+      for (int t = t0; t < t0 + 32; ++t) {
+        acc += stg<Tin>(sm, IN_W, t, k);
+        Grow[t * RS + k] = acc;
+      }
+    } else {
+      const int v = tid & 63, t0 = ((tid - 128) >> 6) * 32;
+#pragma unroll
+      for (int t = t0; t < t0 + 32; t += 4) {
+        kst4(sm + S_VT, v, t,
+             make_float4(stg<Tin>(sm, IN_V, t, v), stg<Tin>(sm, IN_V, t + 1, v),
+                         stg<Tin>(sm, IN_V, t + 2, v), stg<Tin>(sm, IN_V, t + 3, v)));
+      }
+    }
+    __syncthreads();
+    if (tid < 128) {
+      const int k = tid & 63;
+      const float mid = Grow[31 * RS + k];
+      if (tid < 64) {
+        s_ref[k] = mid;
+        s_eref[k] = __expf(mid);
       } else {
-        const int t = drow - 64;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int s = (cb & 1) * 32 + i;
-          const float x = (s <= t) ? vals[i] : 0.f;
-          if (kcols) kst(sm + R3 + TILE, t, s, x);  // A_qk
-          else kst(sm + R4, t, s, x);               // A_qb
-        }
+#pragma unroll 8
+        for (int t = 32; t < 64; ++t) Grow[t * RS + k] += mid;
+        const float gc = Grow[63 * RS + k];
+        s_gc[k] = __expf(gc);
+        // exp(+-(G - G_mid)) must stay finite in fp32 (e^88); RWKV-7's
+        // decay (w >= -0.61 per token) keeps the span under 20.
+        if (fmaxf(fabsf(Grow[k] - mid), fabsf(gc - mid)) > 80.f)
+          report(p.status, WKVM_ERR_UNSUPPORTED);
       }
+    }
+    __syncthreads();
+
+    // ---- E2: rows. lo rows t: a~ -> TMEM, k~ -> B tile row t, a e^Gx -> AG;
+    //          hi rows t: r~ -> TMEM, b~ -> B tile row 64+t, r e^G -> TMEM.
+    {
+      const int t = r64;
+      float av[32], xg[32];
+#pragma unroll
+      for (int k8 = 0; k8 < 32; k8 += 8) {
+        const int k0 = c0 + k8;
+        float x[8], wv[8], y[8], z[8], gt[8];
+        stg8<Tin>(sm, IN_W, t, k0, wv);
+        stg8<Tin>(sm, IN_5, t, k0, x);
+        if (lo) {
+          stg8<Tin>(sm, IN_K, t, k0, y);
+        } else {
+          stg8<Tin>(sm, IN_R, t, k0, y);
+          stg8<Tin>(sm, IN_6, t, k0, z);
+        }
+        *reinterpret_cast<float4*>(&gt[0]) = *reinterpret_cast<const float4*>(&Grow[t * RS + k0]);
+        *reinterpret_cast<float4*>(&gt[4]) = *reinterpret_cast<const float4*>(&Grow[t * RS + k0 + 4]);
+        float bt[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int k = k0 + i;
+          const float ref = s_ref[k];
+          const float er = s_eref[k];
+          const float e = __expf(gt[i] - ref);  // e^{G - g0}
+          const float einv = __frcp_rn(e);       // e^{g0 - G}
+          if (lo) {
+            const float a = MUL ? -x[i] : x[i];
+            const float ea = a * e * __expf(-wv[i]);  // a e^{Gx - g0}
+            av[k8 + i] = ea;
+            xg[k8 + i] = ea * er;                       // a e^{Gx}
+            bt[i] = y[i] * einv;                        // k~
+          } else {
+            const float rr = y[i] * p.scale * e;       // r~
+            av[k8 + i] = rr;
+            xg[k8 + i] = rr * er;                       // r e^G
+            const float b = MUL ? x[i] * z[i] : z[i];
+            bt[i] = b * einv;                           // b~
+          }
+        }
+        kst4(sm + S_RB, l, k0, make_float4(bt[0], bt[1], bt[2], bt[3]));
+        kst4(sm + S_RB, l, k0 + 4, make_float4(bt[4], bt[5], bt[6], bt[7]));
+      }
+      tc::tmem_st32(tq + T_A1 + c0, av);
+      if (lo) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) st4(&AG[t * RS + c0 + i], &xg[i]);
+      } else {
+        tc::tmem_st32(tq + T_RG + c0, xg);
+      }
+      tc::tmem_st_wait();
     }
     sync_tc();
 
-    // ---- MMA 2: [A_ak; A_qk] x V -> TMEM cols [128, 192) (top half used)
+    // ---- MMA 1: [a~; r~](TMEM) x [k~; b~]^T -> D1
     if (tid == 0) {
-      const uint32_t id = tc::idesc_tf32(128, 64);
-      const uint32_t a0 = tc::smem_u32(sm + R3), b0 = tc::smem_u32(sm + R5);
-      for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32(tm + 128, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO),
-                     tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), id, kk > 0);
+      const uint32_t b0 = tc::smem_u32(sm + S_RB);
+      for (int kk = 0; kk < HD / 8; ++kk)
+        tc::mma_tf32_ta(tm + T_D1, tm + T_A1 + kk * 8,
+                        tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), idesc128, kk > 0);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
-    if (warp < 2) {
+
+    // ---- mask in place: rows t of the top half keep s < t, bottom s <= t;
+    //      A_ab (top, right half) goes to shared memory for the solve.
+    {
+      const int t = r64;
 #pragma unroll 1
-      for (int cb = 0; cb < 2; ++cb) {
-        float vals[32];
-        tc::tmem_ld32(tc::tmem_addr(tm, warp * 32, 128 + cb * 32), vals);
+      for (int h2 = 0; h2 < 2; ++h2) {  // h2 = 0: x k~ columns, 1: x b~ columns
+        float x[32];
+        const uint32_t ta = tq + T_D1 + h2 * 64 + c0;
+        tc::tmem_ld32(ta, x);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) AkV[drow * 64 + cb * 32 + i] = vals[i];
+        for (int i = 0; i < 32; ++i) {
+          const int s = c0 + i;
+          const bool keep = lo ? (s < t) : (s <= t);
+          x[i] = keep ? x[i] : 0.f;
+        }
+        if (lo && h2 == 1) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) st4(&Aab[t * RS + c0 + i], &x[i]);
+        } else {
+          tc::tmem_st32(ta, x);
+        }
       }
+      tc::tmem_st_wait();
+    }
+    sync_tc();
+
+    // ---- MMA 2: [A_ak; A_qk](TMEM) x V -> cols T_A1 (top half = A_ak V)
+    if (tid == 0) {
+      const uint32_t b0 = tc::smem_u32(sm + S_VT);
+      for (int kk = 0; kk < CH / 8; ++kk)
+        tc::mma_tf32_ta(tm + T_A1, tm + T_D1 + kk * 8,
+                        tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
+      tc::mma_commit(&mbar);
+    }
+    if (!wait_mma()) { failed = true; break; }
+
+    // ---- lo rows: A_ak V -> shared memory; Kh^T, Bh^T (row k, tokens of this
+    //      thread's half) -> TMEM lanes k of D1's two halves (A_ak, A_ab spent).
+    if (lo) {
+      const int k = r64;
+      float x[32];
+      tc::tmem_ld32(tq + T_A1 + c0, x);
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) st4(&AkV[k * RS + c0 + i], &x[i]);
+      const float gc = Grow[63 * RS + k];
+      float bh[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int t = c0 + i;
+        const float e = __expf(gc - Grow[t * RS + k]);
+        x[i] = stg<Tin>(sm, IN_K, t, k) * e;
+        bh[i] = in_b<Tin, MUL>(sm, t, k) * e;
+      }
+      tc::tmem_st32(tq + T_D1 + c0, x);
+      tc::tmem_st32(tq + T_D1 + 64 + c0, bh);
+      tc::tmem_st_wait();
     }
     tc::fence_before_sync();
     __syncthreads();
+    tc::fence_after_sync();
 
-    // ---- forward substitution: (I - A_ab) y = rhs, one column per thread
-    {
+    // ---- forward substitution (I - A_ab) y = rhs, one column per thread of
+    //      warps 0-3: W (rhs a e^Gx) for tid < 64, U~ (rhs A_ak V) above.
+    //      Rows go in blocks of 8: the contributions of earlier blocks are 8
+    //      independent dot products, then an 8-row triangular finish.
+    if (tid < 128) {
       const int col = tid & 63;
-      const float* rhs = (tid < 64) ? ag : AkV;
+      const float* rhs = (tid < 64) ? AG : AkV;
       float y[CH];
 #pragma unroll
-      for (int t = 0; t < CH; ++t) {
-        float a0 = rhs[t * 64 + col], a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (int b = 0; b < CH / 8; ++b) {
+        float acc[8];
 #pragma unroll
-        for (int s = 0; s + 4 <= t; s += 4) {
-          const float4 av = *reinterpret_cast<const float4*>(&Arow[t * 64 + s]);
-          a0 = fmaf(av.x, y[s], a0);
-          a1 = fmaf(av.y, y[s + 1], a1);
-          a2 = fmaf(av.z, y[s + 2], a2);
-          a3 = fmaf(av.w, y[s + 3], a3);
+        for (int i = 0; i < 8; ++i) acc[i] = rhs[(8 * b + i) * RS + col];
+#pragma unroll
+        for (int s = 0; s < 8 * b; s += 4) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 a4 = *reinterpret_cast<const float4*>(&Aab[(8 * b + i) * RS + s]);
+            acc[i] = fmaf(a4.x, y[s], acc[i]);
+            acc[i] = fmaf(a4.y, y[s + 1], acc[i]);
+            acc[i] = fmaf(a4.z, y[s + 2], acc[i]);
+            acc[i] = fmaf(a4.w, y[s + 3], acc[i]);
+          }
         }
 #pragma unroll
-        for (int s = t & ~3; s < t; ++s) a0 = fmaf(Arow[t * 64 + s], y[s], a0);
-        y[t] = (a0 + a1) + (a2 + a3);
-      }
-      uint8_t* dst = sm + R2 + (tid < 64 ? 0 : TILE);  // W^T | U~^T, row = column index
+        for (int i = 0; i < 8; ++i) {
+          float v = acc[i];
 #pragma unroll
-      for (int t = 0; t < CH; t += 4) kst4(dst, col, t, make_float4(y[t], y[t + 1], y[t + 2], y[t + 3]));
+          for (int s = 8 * b; s < 8 * b + i; ++s) v = fmaf(Aab[(8 * b + i) * RS + s], y[s], v);
+          y[8 * b + i] = v;
+        }
+      }
+      // [W^T; U~^T]: row tid, K = t (the [k~; b~] tile was consumed by MMA 1)
+#pragma unroll
+      for (int t = 0; t < CH; t += 4)
+        kst4(sm + S_RB, tid, t, make_float4(y[t], y[t + 1], y[t + 2], y[t + 3]));
     }
     sync_tc();
 
-    // ---- MMA 3: [A_qb; Bh^T] x [W | U~] -> cols [0,128); += [A_qk; Kh^T] x V -> cols [64,128)
+    // ---- MMA 3a: [Bh^T; A_qb] x W -> T_A1 ; MMA 3b: [Bh^T; A_qb] x U~
+    //      + [Kh^T; A_qk] x V -> T_D3
     if (tid == 0) {
-      const uint32_t id128 = tc::idesc_tf32(128, 128), id64 = tc::idesc_tf32(128, 64);
-      const uint32_t a0 = tc::smem_u32(sm + R4), b0 = tc::smem_u32(sm + R2);
+      const uint32_t w0 = tc::smem_u32(sm + S_RB);
+      const uint32_t u0 = w0 + 8 * SBO;
+      const uint32_t v0 = tc::smem_u32(sm + S_VT);
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32(tm, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO),
-                     tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), id128, kk > 0);
-      const uint32_t a1 = tc::smem_u32(sm + R3 + TILE), b1 = tc::smem_u32(sm + R5);
+        tc::mma_tf32_ta(tm + T_A1, tm + T_D1 + 64 + kk * 8,
+                        tc::smem_desc(w0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32(tm + 64, tc::smem_desc(a1 + kk * KSTEP, LBO, SBO),
-                     tc::smem_desc(b1 + kk * KSTEP, LBO, SBO), id64, true);
+        tc::mma_tf32_ta(tm + T_D3, tm + T_D1 + 64 + kk * 8,
+                        tc::smem_desc(u0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
+      for (int kk = 0; kk < CH / 8; ++kk)
+        tc::mma_tf32_ta(tm + T_D3, tm + T_D1 + kk * 8,
+                        tc::smem_desc(v0 + kk * KSTEP, LBO, SBO), idesc64, true);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
 
-    // ---- P = r e^G + A_qb W ; M = diag(e^G_C) + Bh^T W  -> [P; M] in R1
-#pragma unroll 1
-    for (int cb = 0; cb < 2; ++cb) {
-      float vals[32];
-      tc::tmem_ld32(tc::tmem_addr(tm, warp * 32, cb * 32), vals);
-      if (drow < 64) {
-        const int t = drow;
+    // ---- M = diag(e^G_C) + Bh^T W (lanes k), P = r e^G + A_qb W (lanes 64+t)
+    {
+      float x[32];
+      const uint32_t ta = tq + T_A1 + c0;
+      tc::tmem_ld32(ta, x);
+      if (lo) {
+        const int k = r64;
+        const float d = s_gc[k];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int j = cb * 32 + i;
-          kst(sm + R1, t, j, rg[t * 64 + j] + vals[i]);
-        }
+        for (int i = 0; i < 32; ++i) x[i] += (c0 + i == k) ? d : 0.f;
       } else {
-        const int kr = drow - 64;
+        float rg[32];
+        tc::tmem_ld32(tq + T_RG + c0, rg);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int j = cb * 32 + i;
-          kst(sm + R1 + TILE, kr, j, vals[i] + (j == kr ? s_gc[kr] : 0.f));
-        }
+        for (int i = 0; i < 32; ++i) x[i] += rg[i];
       }
+      tc::tmem_st32(ta, x);
+      tc::tmem_st_wait();
     }
     sync_tc();
 
-    // ---- MMA 4: [O; S'] = [P; M] x S + [O_intra; N] (accumulate on cols [64,128))
+    // ---- MMA 4: [S'; O] = [M; P] x S + [N; O_intra]
     if (tid == 0) {
-      const uint32_t id = tc::idesc_tf32(128, 64);
-      const uint32_t a0 = tc::smem_u32(sm + R1), b0 = tc::smem_u32(sm + R6);
+      const uint32_t s0 = tc::smem_u32(sm + S_ST);
       for (int kk = 0; kk < HD / 8; ++kk)
-        tc::mma_tf32(tm + 64, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO),
-                     tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), id, true);
+        tc::mma_tf32_ta(tm + T_D3, tm + T_A1 + kk * 8,
+                        tc::smem_desc(s0 + kk * 2 * LBO_S, LBO_S, SBO_S), idesc64, true);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
 
-#pragma unroll 1
-    for (int cb = 0; cb < 2; ++cb) {
-      float vals[32];
-      tc::tmem_ld32(tc::tmem_addr(tm, warp * 32, 64 + cb * 32), vals);
-      if (drow < 64) {
-        const int t = drow;
-        if (t < clen) store_row32(go + ((tok0 + t) * H + hh) * HD + cb * 32, vals);
-      } else {
-        const int kr = drow - 64;
+    {
+      float x[32];
+      tc::tmem_ld32(tq + T_D3 + c0, x);
+      if (lo) {
+        const int k = r64;  // S'[k][v]: column k of S^T
 #pragma unroll
-        for (int i = 0; i < 32; ++i) kst(sm + R6, cb * 32 + i, kr, vals[i]);
+        for (int i = 0; i < 32; ++i)
+          *reinterpret_cast<float*>(sm + S_ST + tc::kmajor_off(c0 + i, k, LBO_S, SBO_S)) = x[i];
         if (last && p.h_out) {
-          float* dst = p.h_out + hoff + kr * 64 + cb * 32;
+          float* dst = p.h_out + hoff + k * HD + c0;
 #pragma unroll
           for (int i = 0; i < 32; i += 4)
-            st_stream_f4(dst + i, make_float4(vals[i], vals[i + 1], vals[i + 2], vals[i + 3]));
+            st_stream_f4(dst + i, make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
         }
+      } else {
+        const int t = r64;
+        if (t < clen) store_row32(go + ((tok0 + t) * H + hh) * HD + c0, x);
       }
     }
     sync_tc();
@@ -414,16 +540,6 @@ int launch_chunk_t(const ChunkArgs& a, int nblocks, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? WKVM_OK : WKVM_ERR_CUDA;
 }
 
-template <bool MUL>
-int launch_chunk(const ChunkArgs& a, int nblocks, int dtype, cudaStream_t stream) {
-  switch (dtype) {
-    case WKVM_DTYPE_F32: return launch_chunk_t<float, MUL>(a, nblocks, stream);
-    case WKVM_DTYPE_BF16: return launch_chunk_t<__nv_bfloat16, MUL>(a, nblocks, stream);
-    case WKVM_DTYPE_F16: return launch_chunk_t<__half, MUL>(a, nblocks, stream);
-    default: return WKVM_ERR_DTYPE;
-  }
-}
-
 bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
 
 }  // namespace
@@ -437,21 +553,40 @@ extern "C" int wkvm_wkv7_decode_slots(const void*, const void*, const void*, con
                                       const void*, const void*, void*, float*, int64_t,
                                       const int32_t*, int32_t, int32_t, int32_t, int32_t,
                                       int32_t, int32_t, int32_t*, wkvm_stream_t);
+extern "C" int wkvm_fused_mul_recurrent_rwkv7(const void*, const void*, const void*, const void*,
+                                              const void*, const void*, void*, const float*,
+                                              float*, const int64_t*, int32_t, int32_t, int32_t,
+                                              int32_t, int32_t, float, int32_t, int32_t*,
+                                              wkvm_stream_t);
+
+namespace {
+// The tensor-core path stages 16-bit rows with 16-byte copies.
+bool chunk_path_ok(int K, int V, int dtype, const void* const* ptrs, int n) {
+  if (K != 64 || V != 64) return false;
+  if (dtype != WKVM_DTYPE_BF16 && dtype != WKVM_DTYPE_F16) return false;
+  for (int i = 0; i < n; ++i)
+    if (!wkvm::al16(ptrs[i])) return false;
+  return true;
+}
+}  // namespace
 
 extern "C" int wkvm_chunk_dplr(const void* r, const void* w, const void* k, const void* v,
                                const void* a, const void* b, void* o, const float* h0,
                                float* ht, const int64_t* cu_seqlens, int32_t B, int32_t T,
                                int32_t H, int32_t K, int32_t V, float scale, int32_t dtype,
                                int32_t* status, wkvm_stream_t stream) {
-  if (K != 64 || V != 64)  // other head sizes run the recurrent kernel
+  const void* ptrs[7] = {r, w, k, v, a, b, o};
+  if (!chunk_path_ok(K, V, dtype, ptrs, 7))  // other shapes/dtypes: recurrent kernel
     return wkvm_fused_recurrent_dplr(r, w, k, v, a, b, o, h0, ht, cu_seqlens, B, T, H, K, V,
                                      scale, dtype, status, stream);
   if (B < 0 || T < 0 || H <= 0) return WKVM_ERR_INVALID_ARG;
   if (B == 0) return WKVM_OK;
   if (!r || !w || !k || !v || !a || !b || !o) return WKVM_ERR_INVALID_ARG;
-  if ((h0 && !wkvm::al16(h0)) || (ht && !wkvm::al16(ht)) || !wkvm::al16(o)) return WKVM_ERR_ALIGN;
+  if ((h0 && !wkvm::al16(h0)) || (ht && !wkvm::al16(ht))) return WKVM_ERR_ALIGN;
   wkvm::ChunkArgs args{r, w, k, v, a, b, o, h0, ht, nullptr, 0, cu_seqlens, T, H, scale, status};
-  return wkvm::launch_chunk<false>(args, B * H, dtype, (cudaStream_t)stream);
+  if (dtype == WKVM_DTYPE_BF16)
+    return wkvm::launch_chunk_t<__nv_bfloat16, false>(args, B * H, (cudaStream_t)stream);
+  return wkvm::launch_chunk_t<__half, false>(args, B * H, (cudaStream_t)stream);
 }
 
 extern "C" int wkvm_wkv7_prefill_slots(const void* r, const void* w, const void* k, const void* v,
@@ -461,16 +596,18 @@ extern "C" int wkvm_wkv7_prefill_slots(const void* r, const void* w, const void*
                                        int32_t K, int32_t V, int32_t dtype, int32_t* status,
                                        wkvm_stream_t stream) {
   if (!bank_layer || num_slots <= 0 || (B > 0 && !slot_ids)) return WKVM_ERR_INVALID_ARG;
-  if (K != 64 || V != 64) {
-    if (cu_seqlens) return WKVM_ERR_SHAPE;
+  const void* ptrs[7] = {r, w, k, v, kk, a, o};
+  if (!chunk_path_ok(K, V, dtype, ptrs, 7)) {
+    if (cu_seqlens) return WKVM_ERR_UNSUPPORTED;
     return wkvm_wkv7_decode_slots(r, w, k, v, kk, a, o, bank_layer, num_slots, slot_ids, B, T,
                                   H, K, V, dtype, status, stream);
   }
   if (B < 0 || T < 0 || H <= 0) return WKVM_ERR_INVALID_ARG;
   if (B == 0) return WKVM_OK;
-  if (!r || !w || !k || !v || !kk || !a || !o) return WKVM_ERR_INVALID_ARG;
-  if (!wkvm::al16(bank_layer) || !wkvm::al16(o)) return WKVM_ERR_ALIGN;
+  if (!wkvm::al16(bank_layer)) return WKVM_ERR_ALIGN;
   wkvm::ChunkArgs args{r, w, k, v, kk, a, o, bank_layer, bank_layer, slot_ids, num_slots,
                        cu_seqlens, T, H, 1.0f, status};
-  return wkvm::launch_chunk<true>(args, B * H, dtype, (cudaStream_t)stream);
+  if (dtype == WKVM_DTYPE_BF16)
+    return wkvm::launch_chunk_t<__nv_bfloat16, true>(args, B * H, (cudaStream_t)stream);
+  return wkvm::launch_chunk_t<__half, true>(args, B * H, (cudaStream_t)stream);
 }
