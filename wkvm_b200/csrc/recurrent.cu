@@ -121,16 +121,31 @@ wkv7_recurrent_kernel(const Tin* __restrict__ r, const Tin* __restrict__ w,
     for (int j = 0; j < ROWS; ++j) hreg[j] = f4_zero();
   }
 
+  // Token inputs are prefetched one step ahead into registers so the global
+  // load latency of token t+1 overlaps the math of token t.
+  Tin nx[6];
+  auto fetch = [&](int64_t t) {
+    const int64_t b = ((sr.bos + t) * H + hh) * (int64_t)N + tid;
+    nx[0] = r[b];
+    nx[1] = w[b];
+    nx[2] = k[b];
+    nx[3] = v[b];
+    nx[4] = x5[b];
+    nx[5] = x6[b];
+  };
+  if (tid < N && sr.len > 0) fetch(0);
+
   for (int64_t t = 0; t < sr.len; ++t) {
     const int buf = (int)(t & 1);
     const int64_t base = ((sr.bos + t) * H + hh) * (int64_t)N;
     if (tid < N) {
-      const float rr = to_f32(r[base + tid]) * scale;
-      const float ew = expf(to_f32(w[base + tid]));
-      const float kv = to_f32(k[base + tid]);
-      const float vv = to_f32(v[base + tid]);
-      const float p5 = to_f32(x5[base + tid]);
-      const float p6 = to_f32(x6[base + tid]);
+      const float rr = to_f32(nx[0]) * scale;
+      const float ew = expf(to_f32(nx[1]));
+      const float kv = to_f32(nx[2]);
+      const float vv = to_f32(nx[3]);
+      const float p5 = to_f32(nx[4]);
+      const float p6 = to_f32(nx[5]);
+      if (t + 1 < sr.len) fetch(t + 1);
       const float aa = MUL_FORM ? -p5 : p5;
       const float bb = MUL_FORM ? p5 * p6 : p6;
       s_in[buf][0][tid] = ew;
@@ -251,14 +266,31 @@ gdn_recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
     for (int j = 0; j < ROWS; ++j) hreg[j] = f4_zero();
   }
 
+  // Inputs of token t+1 are fetched into registers while token t computes.
+  Tin nq = Tin(), nk = Tin(), nv = Tin(), ng = Tin(), nb = Tin();
+  auto fetch = [&](int64_t t) {
+    const int64_t tk = sr.bos + t;
+    if (tid < K) {
+      nq = q[(tk * H + hq) * (int64_t)K + tid];
+      nk = k[(tk * H + hq) * (int64_t)K + tid];
+    }
+    if (tid < V) nv = v[(tk * HV + hv) * (int64_t)V + tid];
+    ng = g[tk * HV + hv];
+    nb = beta[tk * HV + hv];
+  };
+  if (sr.len > 0) fetch(0);
+
   for (int64_t t = 0; t < sr.len; ++t) {
     const int buf = (int)(t & 1);
     const int64_t tok = sr.bos + t;
-    const int64_t qk_base = (tok * H + hq) * (int64_t)K;
     const int64_t v_base = (tok * HV + hv) * (int64_t)V;
+    const float cur_v = to_f32(nv);
+    const float cur_g = to_f32(ng);
+    const float cur_b = to_f32(nb);
+    const float qq = to_f32(nq);
+    const float kv = to_f32(nk);
+    if (t + 1 < sr.len) fetch(t + 1);
     if (tid < K) {
-      const float qq = to_f32(q[qk_base + tid]);
-      const float kv = to_f32(k[qk_base + tid]);
       s_qk[buf][0][tid] = qq;
       s_qk[buf][1][tid] = kv;
       const float d_qq = warp_sum<32>(qq * qq);
@@ -270,9 +302,9 @@ gdn_recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
         s_dot[buf][tid >> 5][2] = d_qk;
       }
     }
-    if (tid < V) s_v[buf][tid] = to_f32(v[v_base + tid]);
-    const float eg = expf(to_f32(g[tok * HV + hv]));
-    const float bt = to_f32(beta[tok * HV + hv]);
+    if (tid < V) s_v[buf][tid] = cur_v;
+    const float eg = expf(cur_g);
+    const float bt = cur_b;
     __syncthreads();
 
     float4 pk = f4_zero(), pq = f4_zero();
