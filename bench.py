@@ -201,34 +201,51 @@ def run_ours(args, world, rank, local):
     ops.check_device_status(dev)
 
     # ---- end-to-end through the public op with host buffers ----
-    host_in = [[t.cpu().pin_memory() for t in layer_in] for layer_in in inputs]
-    host_out = [torch.empty_like(o, device="cpu").pin_memory() for o in outs]
-    dev_in = [[torch.empty_like(t) for t in layer_in] for layer_in in inputs]
-    ids_list = ids_host.tolist()
-    h2d = sum(t.numel() * t.element_size() for li in host_in for t in li) + 4 * ACTIVE
-    d2h = sum(o.numel() * o.element_size() for o in host_out)
+    # Per layer: pinned-host inputs -> device on a copy stream, the op on the
+    # compute stream once that layer's copy landed, o -> pinned host after it.
+    e2e_ms, h2d, d2h, e_steps = None, 0, 0, max(1, args.steps)
+    if not args.no_e2e:
+        host_in = [[t.cpu().pin_memory() for t in layer_in] for layer_in in inputs]
+        host_out = [torch.empty_like(o, device="cpu").pin_memory() for o in outs]
+        dev_in = [[torch.empty_like(t) for t in layer_in] for layer_in in inputs]
+        ids_list = ids_host.tolist()
+        h2d = sum(t.numel() * t.element_size() for li in host_in for t in li) + 4 * ACTIVE
+        d2h = sum(o.numel() * o.element_size() for o in host_out)
+        comp = torch.cuda.current_stream(dev)
+        copy = torch.cuda.Stream(dev)
+        in_ev = [torch.cuda.Event() for _ in range(L)]
+        out_ev = [torch.cuda.Event() for _ in range(L)]
 
-    def e2e_step():
-        dids = ops.slot_ids_tensor(ids_list, NUM_SLOTS + 1, dev)
-        for layer in range(L):
-            for d, hsrc in zip(dev_in[layer], host_in[layer]):
-                d.copy_(hsrc, non_blocking=True)
-            o = ops.wkv7_decode_slots(*dev_in[layer], bank.wkv, layer, dids)
-            host_out[layer].copy_(o, non_blocking=True)
+        def e2e_step():
+            dids = ops.slot_ids_tensor(ids_list, NUM_SLOTS + 1, dev)
+            copy.wait_stream(comp)
+            with torch.cuda.stream(copy):
+                for layer in range(L):
+                    for d, hsrc in zip(dev_in[layer], host_in[layer]):
+                        d.copy_(hsrc, non_blocking=True)
+                    in_ev[layer].record(copy)
+            for layer in range(L):
+                comp.wait_event(in_ev[layer])
+                ops.wkv7_decode_slots(*dev_in[layer], bank.wkv, layer, dids, out=outs[layer])
+                out_ev[layer].record(comp)
+            with torch.cuda.stream(copy):
+                for layer in range(L):
+                    copy.wait_event(out_ev[layer])
+                    host_out[layer].copy_(outs[layer], non_blocking=True)
+            comp.wait_stream(copy)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    e_steps = max(1, args.steps)
-    s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(e_steps):
-        e2e_step()
-    t2.record()
-    torch.cuda.synchronize(dev)
-    e2e_ms = max_over_ranks(s2.elapsed_time(t2), world, dev)
-    ops.check_device_status(dev)
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(e_steps):
+            e2e_step()
+        t2.record()
+        torch.cuda.synchronize(dev)
+        e2e_ms = max_over_ranks(s2.elapsed_time(t2), world, dev)
+        ops.check_device_status(dev)
 
     if rank != 0:
         return None
@@ -253,12 +270,12 @@ def run_ours(args, world, rank, local):
         "dtype": "bf16 in/out, fp32 state",
         "data": "synthetic (seeded, reference op-level distributions)",
         "config": {
-            "workload": "RWKV-7 1.5B-shape WKV slot decode: L=24 H=32 N=64, 256 active of "
+            "workload": f"RWKV-7 1.5B-shape WKV slot decode: L={L} H=32 N=64, 256 active of "
                         "1024 arena slots per GPU, all layers per step",
             "global_batch": ACTIVE * world,
             "slots_per_gpu": NUM_SLOTS,
             "parallelism": f"slot-sharded x{world}, no collective",
-            "graph": "CUDA graph of 24 per-layer launches",
+            "graph": f"CUDA graph of {L} per-layer launches",
             "l2": "no flush: 6.4 GB state traffic per step > 126 MB L2",
         },
         "roofline": {
@@ -274,17 +291,80 @@ def run_ours(args, world, rank, local):
         },
         "clocks": clk.summary(),
         "gpu_launches": L * args.steps,
-        "e2e": {
+        "e2e": None if e2e_ms is None else {
             "value": round(world * ACTIVE * e_steps / (e2e_ms * 1e-3), 1),
             "unit": "tokens/s",
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "path": "ops.wkv7_decode_slots with pinned-host inputs/outputs and host slot ids",
+            "path": "ops.wkv7_decode_slots with pinned-host inputs/outputs and host slot ids; "
+                    "per-layer copies on a copy stream overlap the previous layer's op",
         },
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_sample_slots)
     return line
+
+
+def run_prefill(args, world, rank, local):
+    """Chunked RWKV-7 prefill of BASELINE config 2 (B=16 sequences x 4096
+    tokens, H=32, N=64, chunk 64) through wkv7_prefill_slots: initial state
+    read from and final state written to arena slots."""
+    from wkvm_b200 import ops, synth
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, T = args.prefill_batch, 4096
+    bank = torch.zeros(1, B + 1, H, N, N, device=dev)
+    bank.normal_(0.0, 0.1, generator=torch.Generator(device=dev).manual_seed(7 + rank))
+    x = synth.rwkv7_inputs(B, T, H, N, seed=rank, device=dev, state=False)
+    ids = ops.slot_ids_tensor(list(range(1, B + 1)), B + 1, dev)
+    o = torch.empty_like(x["v"])
+    ops.status_word(dev)
+
+    def step():
+        ops.wkv7_prefill_slots(x["r"], x["w"], x["k"], x["v"], x["kk"], x["a"], bank, 0, ids,
+                               out=o)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index if dev.index is not None else 0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        stop.record()
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world, dev)
+    ops.check_device_status(dev)
+    if rank != 0:
+        return None
+    step_ms = ms / args.steps
+    token_heads = B * T * H
+    flops = token_heads * 109.2e3          # WY-form FLOPs per token-head (N = 64, C = 64)
+    byts = token_heads * 896 + 2 * B * H * N * N * 4
+    d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tf32_peak = d.get("bf16_tflops", 1590.0) / 2  # tf32 dense = half the bf16 rate
+    hbm_peak, _ = peaks()
+    return {
+        "metric": "WKV-7 chunked prefill tokens/s (BASELINE config 2)",
+        "value": round(world * B * T * args.steps / (ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 in/out, tf32 tensor-core operands, fp32 state",
+        "data": "synthetic (seeded, reference op-level distributions)",
+        "config": {"workload": f"B={B} T={T} H=32 N=64 chunk 64, state in arena slots",
+                   "kernel": "dplr_chunk_kernel (tcgen05 kind::tf32)"},
+        "roofline": {"bound": "hbm", "achieved": round(byts / (step_ms * 1e-3) / 1e9, 1),
+                     "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(byts / (step_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                     "tensor_tflops": round(flops / (step_ms * 1e-3) / 1e12, 2),
+                     "tensor_peak_tflops": tf32_peak,
+                     "tensor_peak_kind": "measured bf16_tflops / 2 (tf32 dense rate)"},
+        "clocks": clk.summary(), "gpu_launches": args.steps,
+    }
 
 
 def _cpu_sample(slots: int, threads: int, seed: int = 0):
@@ -351,16 +431,26 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample-slots", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=24,
+                    help="layers per decode step (24 = the benchmark; fewer for profiling)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--prefill-batch", type=int, default=16)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    global L
+    L = args.layers
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
         line = run_reference(args, world, rank)
     else:
         world, rank, local = dist_setup()
-        line = run_ours(args, world, rank, local)
+        if args.workload == "prefill":
+            line = run_prefill(args, world, rank, local)
+        else:
+            line = run_ours(args, world, rank, local)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()

@@ -336,12 +336,13 @@ def gdn_decode_slots(q, k, v, g, beta, bank: torch.Tensor, layer: int, slot_ids,
 
 
 def wkv7_prefill_slots(r, w, k, v, kk, a, bank_wkv: torch.Tensor, layer: int, slot_ids,
-                       cu_seqlens=None) -> torch.Tensor:
+                       cu_seqlens=None, out: torch.Tensor | None = None) -> torch.Tensor:
     """Chunked RWKV-7 prefill whose initial state is read from, and final
     state written to, bank_wkv[layer, slot_ids] (replaces wkvm's
     RWKV7Runner.prefill gather -> chunk_rwkv7 -> scatter, runner.py:52-62)."""
     from . import prefill
-    return prefill.wkv7_prefill_slots(r, w, k, v, kk, a, bank_wkv, layer, slot_ids, cu_seqlens)
+    return prefill.wkv7_prefill_slots(r, w, k, v, kk, a, bank_wkv, layer, slot_ids, cu_seqlens,
+                                      out=out)
 
 
 def gdn_prefill_slots(q, k, v, g, beta, bank, layer: int, slot_ids, scale=None,
