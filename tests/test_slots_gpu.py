@@ -126,3 +126,32 @@ def test_migrate_same_device_path(cuda):
     assert torch.equal(b.wkv[:, 3], a.wkv[:, 1])
     assert torch.equal(b.shift[:, :, 4], a.shift[:, :, 2])
     assert b.wkv[:, [0, 1, 2, 4]].abs().sum().item() == 0
+
+
+def test_bank_packer_round_trip(cuda):
+    """The device packer used for cross-process migration: rows of both
+    families for n slots -> one flat buffer -> another bank, bit-exact."""
+    from wkvm_b200 import shard
+    a, b = _bank(cuda), _bank(cuda, fill=False)
+    pack, _, _ = shard.bank_packer(a)
+    _, unpack, empty = shard.bank_packer(b)
+    buf = pack([2, 4])
+    assert buf.numel() == empty(2).numel()
+    unpack([1, 3], buf)
+    torch.cuda.synchronize()
+    assert torch.equal(b.wkv[:, 1], a.wkv[:, 2]) and torch.equal(b.wkv[:, 3], a.wkv[:, 4])
+    assert torch.equal(b.shift[:, :, 1], a.shift[:, :, 2])
+    assert torch.equal(b.shift[:, :, 3], a.shift[:, :, 4])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_migrate_between_gpus_peer_stores(cuda):
+    a = _bank(torch.device("cuda", 0))
+    b = RWKV7StateBank(LAYOUT, num_slots=4, device=torch.device("cuda", 1))
+    with torch.cuda.device(0):
+        ev = a.migrate_to(b, [{"wkv": 2, "shift": 3}], [{"wkv": 4, "shift": 1}])
+        ev.synchronize()
+    torch.cuda.synchronize(1)
+    assert torch.equal(b.wkv[:, 4].cpu(), a.wkv[:, 2].cpu())
+    assert torch.equal(b.shift[:, :, 1].cpu(), a.shift[:, :, 3].cpu())
+    assert b.wkv[:, [0, 1, 2, 3]].abs().sum().item() == 0
