@@ -94,7 +94,7 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 template <typename T>
@@ -220,31 +220,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
   const uint32_t idesc64 = tc::idesc_tf32(128, 64);
   const uint32_t idesc128 = tc::idesc_tf32(128, 128);
 
+  // Issues 16-byte async copies of chunk c's six 64 x 64 input tiles into the
+  // staging area (rows past the sequence end are zero-filled).
+  // Thread tid copies piece (tid & 7) of rows t = (tid >> 3) + 32 * (j & 1) of
+  // input stream j >> 1, for j = 0..11.
+  static_assert(NTHREADS == 256 && NIN * CH * 8 == 12 * NTHREADS, "staging map");
+  auto stage = [&](int c) {
+    const int64_t t0 = bos + (int64_t)c * CH;
+    const int64_t rem = len - (int64_t)c * CH;
+    const int cl = rem < CH ? (int)rem : CH;
+    const uint32_t base = tc::smem_u32(sm + S_STG);
+    const int piece = tid & 7;
+    const int trow = tid >> 3;
+    const int64_t gstride = (int64_t)H * HD * 2;  // bytes between tokens
+    const int64_t goff = (t0 * H + hh) * HD * 2 + piece * 16;
+#pragma unroll
+    for (int j = 0; j < 12; ++j) {
+      const int in = j >> 1;
+      const int t = trow + 32 * (j & 1);
+      const uint32_t off = (in * CH + t) * STG_ROW + piece * 16;
+      if (t < cl) cp_async16(base + off, gin[in] + goff + t * gstride);
+      else *reinterpret_cast<uint4*>(sm + S_STG + off) = make_uint4(0, 0, 0, 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (nchunks > 0) stage(0);
+
   for (int c = 0; c < nchunks; ++c) {
     const int64_t tok0 = bos + (int64_t)c * CH;
     const int64_t rem = len - (int64_t)c * CH;
     const int clen = rem < CH ? (int)rem : CH;
     const bool last = (c == nchunks - 1);
 
-    // ---- stage the chunk's raw inputs (one batch of 16-byte async copies)
-    {
-      const uint32_t base = tc::smem_u32(sm + S_STG);
-      constexpr int PIECES = NIN * CH * (HD * 2 / 16);  // 16-byte pieces
-#pragma unroll 4
-      for (int e = tid; e < PIECES; e += NTHREADS) {
-        const int in = e / (CH * 8);
-        const int t = (e / 8) % CH;
-        const int piece = e % 8;
-        const uint32_t off = (in * CH + t) * STG_ROW + piece * 16;
-        if (t < clen) {
-          cp_async16(base + off, gin[in] + (((tok0 + t) * H + hh) * HD) * 2 + piece * 16);
-        } else {
-          *reinterpret_cast<uint4*>(sm + S_STG + off) = make_uint4(0, 0, 0, 0);
-        }
-      }
-      cp_async_wait_all();
-      __syncthreads();
-    }
+    // ---- the chunk's raw inputs were staged by the previous iteration (or
+    //      before the loop); wait for the async copies to land
+    cp_async_wait_all();
+    __syncthreads();
 
     // ---- E1: threads 0..127 scan half a column of w each; 128..255 write V^T
     if (tid < 128) {
@@ -409,6 +420,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
+    // The staged inputs and G are spent: stage the next chunk now so its
+    // copies overlap the rest of this one.
+    if (c + 1 < nchunks) stage(c + 1);
 
     // ---- forward substitution (I - A_ab) y = rhs, one column per thread of
     //      warps 0-3: W (rhs a e^Gx) for tid < 64, U~ (rhs A_ak V) above.
@@ -521,6 +535,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     sync_tc();
   }
 
+  cp_async_wait_all();  // no copy may still target this CTA's shared memory
   if (failed) {
     // an MMA group may still be running: give it a bounded chance to land
     tc::mbar_wait(&mbar, phase ^ 1u);
