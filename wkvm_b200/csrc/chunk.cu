@@ -10,20 +10,21 @@
 // chunk midpoint as a scaling reference, C = the last row):
 //   [a e^(Gx-g0); r e^(G-g0)] x [k e^(g0-G); b e^(g0-G)]^T
 //        -> A_ak (s<t), A_ab (s<t), A_qk (s<=t), A_qb (s<=t)         (MMA 1)
-//   [A_ak; A_qk] x V          (top half = A_ak V)                     (MMA 2)
-//   (I - A_ab) [W | U~] = [a e^Gx | A_ak V]     forward substitution, fp32
+//   V^T x A_ak^T = (A_ak V)^T                                         (MMA 2)
+//   T = (I - A_ab)^-1, blocked 16 -> 32 -> 64 inverse on the CUDA cores
+//   [(A_ak V)^T; (a e^Gx)^T] x T^T = [U~^T; W^T]                      (MMA S)
 //   [Bh^T; A_qb] x W                                                  (MMA 3a)
 //   [Bh^T; A_qb] x U~ + [Kh^T; A_qk] x V = [N; O_intra]               (MMA 3b)
 //        with Kh = k e^(G_C - G), Bh = b e^(G_C - G)
 //   M = diag(e^G_C) + Bh^T W,  P = r e^G + A_qb W
 //   [S'; O] = [M; P] x S + [N; O_intra]                               (MMA 4)
 //
-// Every A operand lives in tensor memory: MMA 1's accumulator is masked in
-// place and fed back as the A operand of MMAs 2 and 3, whose accumulators in
-// turn become MMA 4's A operand, so only B operands go through shared memory.
-// TMEM: [0,64) a~/r~ -> A_ak V -> [M; P]; [64,192) MMA 1's result, later
-// [Kh^T | Bh^T] in its upper lanes; [192,256) [N; O_intra] -> [S'; O];
-// [256,320) r e^G for the output rows.
+// A operands live in tensor memory where they are produced there: MMA 1's
+// accumulator is masked in place and its lower half feeds MMA 3; MMA 2's
+// result, completed by (a e^Gx)^T, feeds MMA S; MMA 3's accumulator becomes
+// MMA 4's A operand. TMEM: [0,64) a~/r~ -> [(A_ak V)^T; (a e^Gx)^T] ->
+// [M; P]; [64,192) MMA 1's result, later [Kh^T | Bh^T] in its upper lanes;
+// [192,256) [U~^T; W^T] -> [N; O_intra] -> [S'; O]; [256,320) r e^G.
 //
 // Algebra and operand orientation are this file's own; the chunk recurrence
 // is the one fla's chunk_dplr_delta_rule implements
@@ -50,10 +51,10 @@ constexpr int STG_ROW = 144;       // bytes per staged 64 x 16-bit input row (+1
 // shared-memory regions (bytes)
 constexpr uint32_t S_STG = 0;                                   // raw inputs [6][64 rows]
 constexpr uint32_t S_G = S_STG + NIN * CH * STG_ROW;            // G row-major (stride RS)
-constexpr uint32_t S_AKV = S_G + CH * RS * 4;                   // A_ak V row-major
-constexpr uint32_t S_AAB = S_AKV + CH * RS * 4;                 // A_ab row-major
-constexpr uint32_t S_AG = S_AAB + CH * RS * 4;                  // a e^Gx row-major
-constexpr uint32_t S_RB = S_AG + CH * RS * 4;                   // [k~; b~] -> [W^T; U~^T]
+constexpr uint32_t S_AK = S_G + CH * RS * 4;                    // A_ak tile (row t, K = s)
+constexpr uint32_t S_AAB = S_AK + CH * RS * 4;                  // A_ab row-major
+constexpr uint32_t S_TT = S_AAB + CH * RS * 4;                  // (I - A_ab)^-1 tile (row t', K = t)
+constexpr uint32_t S_RB = S_TT + CH * RS * 4;                   // [k~; b~] -> [W^T; U~^T]
 constexpr uint32_t S_VT = S_RB + 2 * 8 * SBO;                   // V^T
 constexpr uint32_t S_ST = S_VT + 8 * SBO;                       // S^T (the running state)
 constexpr uint32_t SMEM_USED = S_ST + 8 * SBO_S;
@@ -187,9 +188,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
                           static_cast<const char*>(p.p4), static_cast<const char*>(p.p5)};
   Tin* __restrict__ go = static_cast<Tin*>(p.o);
   float* Grow = reinterpret_cast<float*>(sm + S_G);
-  float* AkV = reinterpret_cast<float*>(sm + S_AKV);
   float* Aab = reinterpret_cast<float*>(sm + S_AAB);
-  float* AG = reinterpret_cast<float*>(sm + S_AG);
 
   if (warp == 0) {
     tc::tmem_alloc(&tmem_slot, TMEM_COLS);
@@ -295,7 +294,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     }
     __syncthreads();
 
-    // ---- E2: rows. lo rows t: a~ -> TMEM, k~ -> B tile row t, a e^Gx -> AG;
+    // ---- E2: rows. lo rows t: a~ -> TMEM, k~ -> B tile row t;
     //          hi rows t: r~ -> TMEM, b~ -> B tile row 64+t, r e^G -> TMEM.
     {
       const int t = r64;
@@ -320,15 +319,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
           const int k = k0 + i;
           const float ref = s_ref[k];
           const float er = s_eref[k];
-          const float e = __expf(gt[i] - ref);  // e^{G - g0}
-          const float einv = __frcp_rn(e);       // e^{g0 - G}
           if (lo) {
             const float a = MUL ? -x[i] : x[i];
-            const float ea = a * e * __expf(-wv[i]);  // a e^{Gx - g0}
+            const float ea = a * __expf(gt[i] - wv[i] - ref);  // a e^{Gx - g0}
+            const float einv = __expf(ref - gt[i]);            // e^{g0 - G}
             av[k8 + i] = ea;
-            xg[k8 + i] = ea * er;                       // a e^{Gx}
+            xg[k8 + i] = 0.f;
             bt[i] = y[i] * einv;                        // k~
           } else {
+            const float e = __expf(gt[i] - ref);       // e^{G - g0}
+            const float einv = __fdividef(1.f, e);     // e^{g0 - G}
             const float rr = y[i] * p.scale * e;       // r~
             av[k8 + i] = rr;
             xg[k8 + i] = rr * er;                       // r e^G
@@ -340,12 +340,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
         kst4(sm + S_RB, l, k0 + 4, make_float4(bt[4], bt[5], bt[6], bt[7]));
       }
       tc::tmem_st32(tq + T_A1 + c0, av);
-      if (lo) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) st4(&AG[t * RS + c0 + i], &xg[i]);
-      } else {
-        tc::tmem_st32(tq + T_RG + c0, xg);
-      }
+      if (!lo) tc::tmem_st32(tq + T_RG + c0, xg);
       tc::tmem_st_wait();
     }
     sync_tc();
@@ -360,8 +355,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     }
     if (!wait_mma()) { failed = true; break; }
 
-    // ---- mask in place: rows t of the top half keep s < t, bottom s <= t;
-    //      A_ab (top, right half) goes to shared memory for the solve.
+    // ---- mask in place: rows t of the top half keep s < t, bottom s <= t.
+    //      A_ak (top, left) -> shared-memory tile (row t, K = s) for MMA 2;
+    //      A_ab (top, right) -> row-major shared memory for the inverse;
+    //      A_qk, A_qb (bottom) stay in TMEM as A operands of MMA 3.
     {
       const int t = r64;
 #pragma unroll 1
@@ -378,6 +375,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
         if (lo && h2 == 1) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4) st4(&Aab[t * RS + c0 + i], &x[i]);
+        } else if (lo) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            kst4(sm + S_AK, t, c0 + i, make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
         } else {
           tc::tmem_st32(ta, x);
         }
@@ -386,35 +387,43 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     }
     sync_tc();
 
-    // ---- MMA 2: [A_ak; A_qk](TMEM) x V -> cols T_A1 (top half = A_ak V)
+    // ---- MMA 2: V^T x A_ak^T -> T_A1 lanes v = (A_ak V)^T. The A operand's
+    //      rows 64..127 run into the next tile (S^T) and give unused rows.
     if (tid == 0) {
-      const uint32_t b0 = tc::smem_u32(sm + S_VT);
+      const uint32_t a0 = tc::smem_u32(sm + S_VT), b0 = tc::smem_u32(sm + S_AK);
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_A1, tm + T_D1 + kk * 8,
-                        tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
+        tc::mma_tf32(tm + T_A1, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO),
+                     tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
 
-    // ---- lo rows: A_ak V -> shared memory; Kh^T, Bh^T (row k, tokens of this
-    //      thread's half) -> TMEM lanes k of D1's two halves (A_ak, A_ab spent).
-    if (lo) {
+    // ---- column phase (thread = column k, tokens of its half):
+    //      lo: Kh^T, Bh^T -> TMEM lanes k of D1's halves (A_ak, A_ab spent);
+    //      hi: (a e^Gx)^T -> T_A1 lanes 64+k, under (A_ak V)^T in lanes 0..63.
+    {
       const int k = r64;
-      float x[32];
-      tc::tmem_ld32(tq + T_A1 + c0, x);
+      float x[32], y[32];
+      if (lo) {
+        const float gc = Grow[63 * RS + k];
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) st4(&AkV[k * RS + c0 + i], &x[i]);
-      const float gc = Grow[63 * RS + k];
-      float bh[32];
+        for (int i = 0; i < 32; ++i) {
+          const int t = c0 + i;
+          const float e = __expf(gc - Grow[t * RS + k]);
+          x[i] = stg<Tin>(sm, IN_K, t, k) * e;
+          y[i] = in_b<Tin, MUL>(sm, t, k) * e;
+        }
+        tc::tmem_st32(tq + T_D1 + c0, x);
+        tc::tmem_st32(tq + T_D1 + 64 + c0, y);
+      } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int t = c0 + i;
-        const float e = __expf(gc - Grow[t * RS + k]);
-        x[i] = stg<Tin>(sm, IN_K, t, k) * e;
-        bh[i] = in_b<Tin, MUL>(sm, t, k) * e;
+        for (int i = 0; i < 32; ++i) {
+          const int t = c0 + i;
+          const float a = stg<Tin>(sm, IN_5, t, k);
+          x[i] = (MUL ? -a : a) * __expf(Grow[t * RS + k] - stg<Tin>(sm, IN_W, t, k));
+        }
+        tc::tmem_st32(tq + T_A1 + c0, x);
       }
-      tc::tmem_st32(tq + T_D1 + c0, x);
-      tc::tmem_st32(tq + T_D1 + 64 + c0, bh);
       tc::tmem_st_wait();
     }
     tc::fence_before_sync();
@@ -424,42 +433,114 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     // copies overlap the rest of this one.
     if (c + 1 < nchunks) stage(c + 1);
 
-    // ---- forward substitution (I - A_ab) y = rhs, one column per thread of
-    //      warps 0-3: W (rhs a e^Gx) for tid < 64, U~ (rhs A_ak V) above.
-    //      Rows go in blocks of 8: the contributions of earlier blocks are 8
-    //      independent dot products, then an 8-row triangular finish.
-    if (tid < 128) {
-      const int col = tid & 63;
-      const float* rhs = (tid < 64) ? AG : AkV;
-      float y[CH];
+    // ---- T = (I - A_ab)^-1 (unit lower triangular), blocked 16 -> 32 -> 64,
+    //      row-major in the G region, then as a K-major tile (row t', K = t).
+    {
+      float* Tr = Grow;
+      if (tid < 64) {  // diagonal 16 x 16 blocks, one column per thread
+        const int col = tid, b0 = col & ~15, ci = col & 15;
+        float y[16];
 #pragma unroll
-      for (int b = 0; b < CH / 8; ++b) {
-        float acc[8];
+        for (int i = 0; i < 16; ++i) {
+          float v = (i == ci) ? 1.f : 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = rhs[(8 * b + i) * RS + col];
-#pragma unroll
-        for (int s = 0; s < 8 * b; s += 4) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 a4 = *reinterpret_cast<const float4*>(&Aab[(8 * b + i) * RS + s]);
-            acc[i] = fmaf(a4.x, y[s], acc[i]);
-            acc[i] = fmaf(a4.y, y[s + 1], acc[i]);
-            acc[i] = fmaf(a4.z, y[s + 2], acc[i]);
-            acc[i] = fmaf(a4.w, y[s + 3], acc[i]);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float v = acc[i];
-#pragma unroll
-          for (int s = 8 * b; s < 8 * b + i; ++s) v = fmaf(Aab[(8 * b + i) * RS + s], y[s], v);
-          y[8 * b + i] = v;
+          for (int i2 = 0; i2 < i; ++i2) v = fmaf(Aab[(b0 + i) * RS + b0 + i2], y[i2], v);
+          y[i] = (i < ci) ? 0.f : v;
+          Tr[(b0 + i) * RS + col] = y[i];
         }
       }
-      // [W^T; U~^T]: row tid, K = t (the [k~; b~] tile was consumed by MMA 1)
+      __syncthreads();
+      {  // blocks (1,0) and (3,2) of 16: X = A T_jj, then T_ij = T_ii X.
+         // Thread: row r = (tid >> 4) & 15, column cc = tid & 15 of both blocks.
+        const int r = (tid >> 4) & 15, cc = tid & 15;
+        float xv[2] = {0.f, 0.f};
 #pragma unroll
-      for (int t = 0; t < CH; t += 4)
-        kst4(sm + S_RB, tid, t, make_float4(y[t], y[t + 1], y[t + 2], y[t + 3]));
+        for (int s2 = 0; s2 < 16; ++s2) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const float tv = Tr[(32 * q + s2) * RS + 32 * q + cc];
+            const float av = Aab[(32 * q + 16 + r) * RS + 32 * q + s2];
+            xv[q] = fmaf(av, s2 >= cc ? tv : 0.f, xv[q]);
+          }
+        }
+        if (tid < 256) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[q];
+        }
+        __syncthreads();
+        float yv[2] = {0.f, 0.f};
+#pragma unroll
+        for (int s2 = 0; s2 < 16; ++s2) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const float tv = Tr[(32 * q + 16 + r) * RS + 32 * q + 16 + s2];
+            const float xx = Tr[(32 * q + 16 + s2) * RS + 32 * q + cc];
+            yv[q] = fmaf(s2 <= r ? tv : 0.f, xx, yv[q]);
+          }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = yv[q];
+      }
+      __syncthreads();
+      {  // block (1,0) of 32: X = A T_00, then T_10 = T_11 X. Thread: column
+         // C = tid & 31, rows 32 + (tid >> 5) + 8 q.
+        const int C = tid & 31, r0 = tid >> 5;
+        float xv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s2 = 0; s2 < 32; ++s2) {
+          const float tv = s2 >= C ? Tr[s2 * RS + C] : 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) xv[q] = fmaf(Aab[(32 + r0 + 8 * q) * RS + s2], tv, xv[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = xv[q];
+        __syncthreads();
+        float yv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s2 = 0; s2 < 32; ++s2) {
+          const float xx = Tr[(32 + s2) * RS + C];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int R = r0 + 8 * q;
+            yv[q] = fmaf(s2 <= R ? Tr[(32 + R) * RS + 32 + s2] : 0.f, xx, yv[q]);
+          }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = yv[q];
+      }
+      __syncthreads();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // K-major tile, zero above the diagonal;
+        // lanes walk 8 rows x 4 K-quads so each store instruction fills 512
+        // contiguous bytes
+        const int e = tid + 256 * q;
+        const int tp = (e >> 7) * 8 + (e & 7), t4 = ((e >> 3) & 15) * 4;
+        float v4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v4[i] = (t4 + i <= tp) ? Tr[tp * RS + t4 + i] : 0.f;
+        kst4(sm + S_TT, tp, t4, make_float4(v4[0], v4[1], v4[2], v4[3]));
+      }
+    }
+    sync_tc();
+
+    // ---- MMA S: [(A_ak V)^T; (a e^Gx)^T] x T^T -> T_D3 = [U~^T; W^T]
+    if (tid == 0) {
+      const uint32_t b0 = tc::smem_u32(sm + S_TT);
+      for (int kk = 0; kk < CH / 8; ++kk)
+        tc::mma_tf32_ta(tm + T_D3, tm + T_A1 + kk * 8,
+                        tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
+      tc::mma_commit(&mbar);
+    }
+    if (!wait_mma()) { failed = true; break; }
+    {  // [W^T; U~^T] B tile: lane l < 64 holds U~^T row l, lane 64+j holds W^T row j
+      float x[32];
+      tc::tmem_ld32(tq + T_D3 + c0, x);
+      const int row = lo ? 64 + l : l - 64;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        kst4(sm + S_RB, row, c0 + i, make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
     }
     sync_tc();
 
