@@ -168,6 +168,10 @@ def run_ours(args, world, rank, local):
     inputs = make_inputs(dev, seed=rank)
     outs = [torch.empty(ACTIVE, 1, H, N, dtype=torch.bfloat16, device=dev) for _ in range(L)]
     ops.status_word(dev)
+    # Consecutive layers overlap their launch tails (programmatic dependent
+    # launch): each launch touches another layer's state, which meets the
+    # op's contract for the overlap mode.
+    ops.set_decode_overlap(not args.no_overlap)
 
     def step():
         for layer in range(L):
@@ -275,7 +279,8 @@ def run_ours(args, world, rank, local):
             "global_batch": ACTIVE * world,
             "slots_per_gpu": NUM_SLOTS,
             "parallelism": f"slot-sharded x{world}, no collective",
-            "graph": f"CUDA graph of {L} per-layer launches",
+            "graph": f"CUDA graph of {L} per-layer launches"
+                     + ("" if args.no_overlap else ", programmatic dependent launch between layers"),
             "l2": "no flush: 6.4 GB state traffic per step > 126 MB L2",
         },
         "roofline": {
@@ -432,6 +437,8 @@ def main():
     ap.add_argument("--cpu-sample-slots", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="plain launches instead of programmatic dependent launch")
     ap.add_argument("--layers", type=int, default=24,
                     help="layers per decode step (24 = the benchmark; fewer for profiling)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])

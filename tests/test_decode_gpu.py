@@ -169,3 +169,33 @@ def test_gdn_decode_slots_long(cuda):
                                    initial_state=h_ref)
     assert_out_close(o, ro)
     assert rel_err(bank[0, ids], rh) < REL_TOL
+
+
+def test_decode_overlap_layer_loop(cuda):
+    """Overlapped (programmatic dependent launch) decode over a layer loop,
+    as a model step issues it, several steps in a row, inside a CUDA graph
+    and eagerly: same results as the oracle run layer by layer."""
+    L, S, H, N, B, steps = 4, 9, 4, 64, 3, 3
+    bank = _bank(L, S, H, N, cuda, seed=4)
+    h_ref = [np32(bank[layer, [5, 1, 7]]) for layer in range(L)]
+    ids = ops.slot_ids_tensor([5, 1, 7], S, cuda)
+    xs = [[_to(synth.rwkv7_inputs(B, 1, H, N, seed=100 * s + layer, state=False), cuda)
+           for layer in range(L)] for s in range(steps)]
+    prev = ops.set_decode_overlap(True)
+    try:
+        outs = []
+        for s in range(steps):
+            outs.append([ops.wkv7_decode_slots(*(xs[s][layer][n] for n in ("r", "w", "k", "v", "kk", "a")),
+                                               bank, layer, ids) for layer in range(L)])
+        torch.cuda.synchronize()
+    finally:
+        ops.set_decode_overlap(prev)
+    for layer in range(L):
+        h = h_ref[layer]
+        for s in range(steps):
+            x = xs[s][layer]
+            ro, h = oracle.rwkv7_recurrence(*(np32(x[n]) for n in ("r", "w", "k", "v", "kk", "a")),
+                                            initial_state=h)
+            assert_out_close(outs[s][layer], ro)
+        assert rel_err(bank[layer, [5, 1, 7]], h) < REL_TOL
+    ops.check_device_status(cuda)

@@ -133,6 +133,13 @@ wkv7_recurrent_kernel(const Tin* __restrict__ r, const Tin* __restrict__ w,
     nx[4] = x5[b];
     nx[5] = x6[b];
   };
+  // Programmatic dependent launch (opt-in for decode, see
+  // wkvm_set_decode_overlap): let the next launch in the stream start its
+  // CTAs now, and wait for the previous launch only here, after the slot ids
+  // and the state were read and before any input is. Without the launch
+  // attribute both instructions are no-ops.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid < N && sr.len > 0) fetch(0);
 
   for (int64_t t = 0; t < sr.len; ++t) {
@@ -387,12 +394,32 @@ struct RecArgs {
   bool l2norm;
   int* status;
   cudaStream_t stream;
+  bool overlap = false;  // programmatic dependent launch (decode only)
 };
+
+// Process-wide opt-in for overlapping consecutive decode launches.
+bool g_decode_overlap = false;
 
 template <int N, int ROWS, typename Tin, bool MUL>
 int launch_wkv7_t(const RecArgs& a) {
   constexpr int NT = (N / 4) * (N / ROWS);
   dim3 grid((unsigned)((int64_t)a.B * a.H));
+  if (a.overlap) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(NT);
+    cfg.stream = a.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(
+        &cfg, wkv7_recurrent_kernel<N, ROWS, Tin, MUL>, (const Tin*)a.p0, (const Tin*)a.p1,
+        (const Tin*)a.p2, (const Tin*)a.p3, (const Tin*)a.p4, (const Tin*)a.p5, (Tin*)a.o,
+        a.h_in, a.h_out, a.ids, a.num_slots, a.cu, a.T, a.H, a.scale, a.status);
+    return e == cudaSuccess ? WKVM_OK : WKVM_ERR_CUDA;
+  }
   wkv7_recurrent_kernel<N, ROWS, Tin, MUL><<<grid, NT, 0, a.stream>>>(
       (const Tin*)a.p0, (const Tin*)a.p1, (const Tin*)a.p2, (const Tin*)a.p3,
       (const Tin*)a.p4, (const Tin*)a.p5, (Tin*)a.o, a.h_in, a.h_out, a.ids, a.num_slots,
@@ -515,6 +542,7 @@ extern "C" int wkvm_wkv7_decode_slots(const void* r, const void* w, const void* 
   if (!bank_layer || (!slot_ids && B > 0) || num_slots <= 0) return WKVM_ERR_INVALID_ARG;
   RecArgs args{r, w, k, v, kk, a, o, bank_layer, bank_layer, slot_ids, num_slots, nullptr,
                B, T, H, H, K, V, 1.0f, false, status, (cudaStream_t)stream};
+  args.overlap = wkvm::g_decode_overlap;
   int rc = wkvm::check_common(args, false);
   if (rc) return rc;
   if (K != V) return WKVM_ERR_SHAPE;
@@ -557,4 +585,10 @@ extern "C" int wkvm_gdn_decode_slots(const void* q, const void* k, const void* v
   if (HV <= 0 || HV % H != 0) return WKVM_ERR_SHAPE;
   if (B == 0 || T == 0) return WKVM_OK;
   return wkvm::launch_gdn(args, dtype);
+}
+
+extern "C" int wkvm_set_decode_overlap(int32_t enable) {
+  const int prev = wkvm::g_decode_overlap ? 1 : 0;
+  wkvm::g_decode_overlap = enable != 0;
+  return prev;
 }

@@ -284,6 +284,15 @@ def _bank_layer(bank: torch.Tensor, layer: int) -> torch.Tensor:
     return bank[layer]
 
 
+def set_decode_overlap(enable: bool) -> bool:
+    """Opt-in overlap of consecutive wkv7_decode_slots launches (programmatic
+    dependent launch). While enabled, the kernel launched right before a
+    decode call on the same stream must not write that call's slot ids or
+    those slots' state in that layer — true for a loop over layers. Returns
+    the previous setting."""
+    return bool(_lib.load().wkvm_set_decode_overlap(int(bool(enable))))
+
+
 def wkv7_decode_slots(r, w, k, v, kk, a, bank_wkv: torch.Tensor, layer: int, slot_ids,
                       out: torch.Tensor | None = None) -> torch.Tensor:
     """RWKV-7 decode of B rows whose states live in bank_wkv[layer, slot_ids]
