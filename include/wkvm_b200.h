@@ -238,6 +238,20 @@ int wkvm_slot_migrate(const void* src_base, void* dst_base, int64_t outer,
 int wkvm_selftest_tf32_mma(const float* A, const float* B, float* D, int32_t N,
                            int32_t a_in_tmem, int32_t* status, wkvm_stream_t stream);
 
+/* State mutation rules on device: for each i, rows of dst_ids[i] <-
+ * c1 * rows(a_ids[i]) + c2 * rows(b_ids[i]) (b_ids NULL: c1 * rows(a_ids[i])),
+ * computed in fp32 with separately rounded products and sum, then rounded to
+ * the family's dtype (dtype = WKVM_DTYPE_*). Bitwise equal to wkvm's
+ * StateStore rules applied with torch: merge (wkvm/store.py:260-268,
+ * c1 = 1 - weight, c2 = weight) and decay (wkvm/store.py:298-305,
+ * c1 = alpha, wkv family only). dst may equal a (in place); a slot may not be
+ * both a destination and a source of another pair in one call. */
+int wkvm_slot_affine(void* base, int64_t outer, int64_t outer_stride,
+                     int64_t slot_stride, int64_t row_bytes, int64_t num_slots,
+                     const int32_t* dst_ids, const int32_t* a_ids, const int32_t* b_ids,
+                     int32_t n, float c1, float c2, int32_t dtype, int32_t* status,
+                     wkvm_stream_t stream);
+
 /* Enables `device` -> `peer` access (cudaDeviceEnablePeerAccess with
  * `device` current); already-enabled counts as success. Needed once per pair
  * before wkvm_slot_migrate writes into the peer's bank. */

@@ -155,3 +155,19 @@ def test_migrate_between_gpus_peer_stores(cuda):
     assert torch.equal(b.wkv[:, 4].cpu(), a.wkv[:, 2].cpu())
     assert torch.equal(b.shift[:, :, 1].cpu(), a.shift[:, :, 3].cpu())
     assert b.wkv[:, [0, 1, 2, 3]].abs().sum().item() == 0
+
+
+def test_mutation_rules_bit_exact(cuda):
+    """decay and merge on live slots equal wkvm's StateStore rules computed
+    by torch on the host copies (wkvm/store.py:260-268, 298-305)."""
+    bank = _bank(cuda)
+    w0, s0 = bank.wkv.cpu(), bank.shift.cpu()
+    bank.decay({"wkv": 2, "shift": 2}, alpha=0.9)
+    assert torch.equal(bank.wkv[:, 2].cpu(), (w0[:, 2].float() * 0.9).to(torch.float32))
+    assert torch.equal(bank.shift.cpu(), s0)
+    bank.merge({"wkv": 4, "shift": 4}, {"wkv": 1, "shift": 1}, {"wkv": 3, "shift": 3}, weight=0.3)
+    ref_w = ((1.0 - 0.3) * w0[:, 1].float() + 0.3 * w0[:, 3].float()).to(torch.float32)
+    ref_s = ((1.0 - 0.3) * s0[:, :, 1].float() + 0.3 * s0[:, :, 3].float()).to(torch.bfloat16)
+    assert torch.equal(bank.wkv[:, 4].cpu(), ref_w)
+    assert torch.equal(bank.shift[:, :, 4].cpu(), ref_s)
+    ops.check_device_status(cuda)

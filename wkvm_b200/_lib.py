@@ -34,6 +34,7 @@ SIGNATURES: dict[str, list] = {
     "wkvm_slot_migrate": [P, P, I64, I64, I64, I64, I64, I64, P, P, I32, P, P],
     "wkvm_enable_peer_access": [I32, I32],
     "wkvm_set_decode_overlap": [I32],
+    "wkvm_slot_affine": [P, I64, I64, I64, I64, I64, P, P, P, I32, F32, F32, I32, P, P],
     "wkvm_selftest_tf32_mma": [P, P, P, I32, I32, P, P],
     "wkvm_chunk_dplr": [P] * 7 + [P, P, P] + [I32] * 5 + [F32, I32, P, P],
     "wkvm_wkv7_prefill_slots": [P] * 7 + [P, I64, P, P] + [I32] * 5 + [I32, P, P],

@@ -79,10 +79,77 @@ int launch_move(MoveArgs a, int64_t n, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? WKVM_OK : WKVM_ERR_CUDA;
 }
 
+// out = fp32(c1 * a) + fp32(c2 * b) per element, rounded once more to the
+// family's dtype; with b absent, out = fp32(c1 * a). Each product and the sum
+// are rounded separately (no fused multiply-add) so the result is bitwise
+// what torch computes for `((1 - w) * a.float() + w * b.float()).to(dtype)`
+// and `(a.float() * alpha).to(dtype)`.
+template <typename T>
+__global__ void __launch_bounds__(256) slot_affine_kernel(char* base, int64_t outer,
+                                                          int64_t outer_stride,
+                                                          int64_t slot_stride, int64_t row_elems,
+                                                          int64_t num_slots,
+                                                          const int32_t* dst_ids,
+                                                          const int32_t* a_ids,
+                                                          const int32_t* b_ids, float c1,
+                                                          float c2, int* status) {
+  const int64_t pair = blockIdx.y;
+  const int64_t d = dst_ids[pair], a = a_ids[pair], b = b_ids ? b_ids[pair] : 0;
+  if (d < 0 || d >= num_slots || a < 0 || a >= num_slots || b < 0 || b >= num_slots) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) report(status, WKVM_ERR_SLOT_RANGE);
+    return;
+  }
+  const int64_t total = outer * row_elems;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = e / row_elems, i = e - o * row_elems;
+    char* ob = base + o * outer_stride;
+    const float x = to_f32(reinterpret_cast<const T*>(ob + a * slot_stride)[i]);
+    float y = __fmul_rn(c1, x);
+    if (b_ids) y = __fadd_rn(y, __fmul_rn(c2, to_f32(reinterpret_cast<const T*>(ob + b * slot_stride)[i])));
+    reinterpret_cast<T*>(ob + d * slot_stride)[i] = from_f32<T>(y);
+  }
+}
+
 }  // namespace
 }  // namespace wkvm
 
 using wkvm::MoveArgs;
+
+extern "C" int wkvm_slot_affine(void* base, int64_t outer, int64_t outer_stride,
+                                int64_t slot_stride, int64_t row_bytes, int64_t num_slots,
+                                const int32_t* dst_ids, const int32_t* a_ids,
+                                const int32_t* b_ids, int32_t n, float c1, float c2,
+                                int32_t dtype, int32_t* status, wkvm_stream_t stream) {
+  if (!base || (n > 0 && (!dst_ids || !a_ids))) return WKVM_ERR_INVALID_ARG;
+  if (n < 0 || outer < 0 || row_bytes < 0 || n > 65535) return WKVM_ERR_INVALID_ARG;
+  if (n == 0 || outer == 0 || row_bytes == 0) return WKVM_OK;
+  const int es = dtype == WKVM_DTYPE_F32 ? 4 : 2;
+  if (row_bytes % es) return WKVM_ERR_ALIGN;
+  const int64_t row_elems = row_bytes / es;
+  const int64_t total = outer * row_elems;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 1184) blocks = 1184;  // 8 resident blocks on each of 148 SMs
+  dim3 grid((unsigned)blocks, (unsigned)n);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case WKVM_DTYPE_F32:
+      wkvm::slot_affine_kernel<float><<<grid, 256, 0, st>>>((char*)base, outer, outer_stride,
+          slot_stride, row_elems, num_slots, dst_ids, a_ids, b_ids, c1, c2, status);
+      break;
+    case WKVM_DTYPE_BF16:
+      wkvm::slot_affine_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((char*)base, outer,
+          outer_stride, slot_stride, row_elems, num_slots, dst_ids, a_ids, b_ids, c1, c2, status);
+      break;
+    case WKVM_DTYPE_F16:
+      wkvm::slot_affine_kernel<__half><<<grid, 256, 0, st>>>((char*)base, outer, outer_stride,
+          slot_stride, row_elems, num_slots, dst_ids, a_ids, b_ids, c1, c2, status);
+      break;
+    default:
+      return WKVM_ERR_DTYPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? WKVM_OK : WKVM_ERR_CUDA;
+}
 
 extern "C" int wkvm_slot_copy(void* base, int64_t outer, int64_t outer_stride,
                               int64_t slot_stride, int64_t row_bytes, int64_t num_slots,

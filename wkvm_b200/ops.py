@@ -479,3 +479,20 @@ def enable_peer_access(src: torch.device, dst: torch.device) -> None:
         raise RuntimeError(f"GPU {src.index} cannot access GPU {dst.index}'s memory")
     _lib.call("wkvm_enable_peer_access", src.index, dst.index)
     _peer_enabled.add(key)
+
+
+def slot_affine(family: torch.Tensor, slot_dim: int, dst_ids, a_ids, b_ids, c1: float,
+                c2: float = 0.0) -> None:
+    """family[.., dst[i], ..] <- c1 * family[.., a[i], ..] + c2 * family[.., b[i], ..]
+    (b_ids None: c1 * a), fp32 arithmetic rounded like torch's elementwise ops."""
+    outer, ostr, sstr, row, ns = _family_geometry(family, slot_dim)
+    d = slot_ids_tensor(dst_ids, ns, family.device)
+    a = slot_ids_tensor(a_ids, ns, family.device, validate=False)
+    b = None if b_ids is None else slot_ids_tensor(b_ids, ns, family.device, validate=False)
+    if a.numel() != d.numel() or (b is not None and b.numel() != d.numel()):
+        raise ValueError("id lists differ in length")
+    dt = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[family.dtype]
+    with torch.cuda.device(family.device):
+        _lib.call("wkvm_slot_affine", _ptr(family), outer, ostr, sstr, row, ns, _ptr(d),
+                  _ptr(a), _ptr(b), d.numel(), float(c1), float(c2), dt,
+                  _ptr(status_word(family.device)), _stream(family.device))

@@ -86,6 +86,19 @@ class RWKV7StateBank:
         ops.slot_copy(self.wkv, 1, _ids(parents, "wkv"), _ids(children, "wkv"))
         ops.slot_copy(self.shift, 2, _ids(parents, "shift"), _ids(children, "shift"))
 
+    # -- mutation rules (wkvm/store.py:260-268, 298-305) on live slots --------
+
+    def decay(self, slots: SlotDict, alpha: float = 0.9) -> None:
+        """wkv <- wkv * alpha in place; token-shift untouched (wkvm's "decay")."""
+        i = [int(slots["wkv"])]
+        ops.slot_affine(self.wkv, 1, i, i, None, float(alpha))
+
+    def merge(self, dst: SlotDict, a: SlotDict, b: SlotDict, weight: float = 0.5) -> None:
+        """Every family: dst <- (1 - weight) * a + weight * b (wkvm's "merge")."""
+        for fam, t, dim in (("wkv", self.wkv, 1), ("shift", self.shift, 2)):
+            ops.slot_affine(t, dim, [int(dst[fam])], [int(a[fam])], [int(b[fam])],
+                            1.0 - float(weight), float(weight))
+
     # -- decode -----------------------------------------------------------
 
     def wkv_decode(self, layer: int, slot_ids, r, w, k, v, kk, a) -> torch.Tensor:
