@@ -179,6 +179,32 @@ int wkvm_wkv7_prefill_slots(
     int32_t B, int32_t T, int32_t H, int32_t K, int32_t V,
     int32_t dtype, int32_t* status, wkvm_stream_t stream);
 
+/* Chunked GDN prefill: replaces fla `chunk_gated_delta_rule`
+ * (fla/ops/gated_delta_rule/chunk.py:365, forward :29-116) for head-wise g
+ * and beta, [K,V] state layout. Arguments as for
+ * wkvm_fused_recurrent_gated_delta_rule. K == V == 128 with 16-bit inputs
+ * runs the tcgen05 tf32 chunk kernel (one CTA per sequence, value head and
+ * half of V); other shapes run the recurrent kernel. */
+int wkvm_chunk_gated_delta_rule(
+    const void* q, const void* k, const void* v, const void* g,
+    const void* beta, void* o,
+    const float* h0, float* ht, const int64_t* cu_seqlens,
+    int32_t B, int32_t T, int32_t H, int32_t HV, int32_t K, int32_t V,
+    float scale, int32_t use_qk_l2norm, int32_t dtype,
+    int32_t* status, wkvm_stream_t stream);
+
+/* Slot-native chunked GDN prefill: initial and final state of sequence i
+ * in bank_layer[slot_ids[i]] ([num_slots, HV, K, V] fp32). No wkvm caller
+ * exists (wkvm runs RWKV-7 only); the operator contract is fla's. */
+int wkvm_gdn_prefill_slots(
+    const void* q, const void* k, const void* v, const void* g,
+    const void* beta, void* o,
+    float* bank_layer, int64_t num_slots, const int32_t* slot_ids,
+    const int64_t* cu_seqlens,
+    int32_t B, int32_t T, int32_t H, int32_t HV, int32_t K, int32_t V,
+    float scale, int32_t use_qk_l2norm, int32_t dtype,
+    int32_t* status, wkvm_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Slot copies. A state family tensor is viewed as [outer, num_slots, row]:
  * bank.wkv [L, S+1, H*K*V fp32] has outer = L; bank.shift [L, 2, S+1, D]

@@ -119,3 +119,57 @@ def test_other_head_dims_use_recurrent_path(cuda):
                                     np32(a), np32(b), initial_state=np32(x["h0"]))
     assert_out_close(o, ro)
     assert rel_err(ht, rh) < REL_TOL
+
+
+GDN = ("q", "k", "v", "g", "beta")
+
+
+@pytest.mark.parametrize("T", [1, 100, 200])
+@pytest.mark.parametrize("hv_mult", [1, 2])
+@pytest.mark.parametrize("l2", [False, True])
+def test_chunk_gdn_matches_oracle(cuda, T, hv_mult, l2):
+    B, H, K = 2, 2, 128
+    x = synth.gdn_inputs(B, T, H, K, HV=H * hv_mult, seed=T + hv_mult)
+    if l2:
+        x["q"] = (x["q"].float() * 2.5).to(torch.bfloat16)
+        x["k"] = (x["k"].float() * 0.7).to(torch.bfloat16)
+    d = _to(x, cuda)
+    o, ht = ops.chunk_gated_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"],
+                                       initial_state=d["h0"], output_final_state=True,
+                                       use_qk_l2norm_in_kernel=l2)
+    ro, rh = oracle.gdn_recurrence(*(np32(x[n]) for n in GDN), initial_state=np32(x["h0"]),
+                                   use_qk_l2norm=l2)
+    ops.check_device_status(cuda)
+    assert_out_close(o, ro)
+    assert rel_err(ht, rh) < REL_TOL
+
+
+def test_chunk_gdn_4096_tokens(cuda):
+    B, T, H, K = 1, 4096, 2, 128
+    x = synth.gdn_inputs(B, T, H, K, seed=31)
+    d = _to(x, cuda)
+    o, ht = ops.chunk_gated_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"],
+                                       initial_state=d["h0"], output_final_state=True)
+    ro, rh = oracle.gdn_recurrence(*(np32(x[n]) for n in GDN), initial_state=np32(x["h0"]))
+    assert_out_close(o, ro)
+    assert rel_err(ht, rh) < REL_TOL
+
+
+def test_gdn_prefill_slots_varlen(cuda):
+    S, HV, K = 6, 2, 128
+    lens = [70, 0, 130]
+    ids = [4, 2, 5]
+    g = torch.Generator().manual_seed(2)
+    bank = (torch.randn(1, S, HV, K, K, generator=g) * 0.1).to(cuda)
+    before = bank.clone()
+    x = synth.gdn_inputs(1, sum(lens), HV, K, seed=3, state=False)
+    d = _to(x, cuda)
+    cu = torch.tensor(np.cumsum([0] + lens), dtype=torch.int64)
+    o = ops.gdn_prefill_slots(*(d[n] for n in GDN), bank, 0, ids, cu_seqlens=cu.to(cuda))
+    ro, rh = oracle.gdn_recurrence(*(np32(x[n]) for n in GDN), initial_state=np32(before[0, ids]),
+                                   cu_seqlens=cu.numpy())
+    ops.check_device_status(cuda)
+    assert_out_close(o, ro)
+    assert rel_err(bank[0, ids], rh) < REL_TOL
+    rest = [0, 1, 3]
+    assert torch.equal(bank[0, rest], before[0, rest]) and torch.equal(bank[0, 2], before[0, 2])

@@ -31,7 +31,7 @@
 // (fla/ops/generalized_delta_rule/dplr/chunk.py:33-135, reference
 // dplr_chunkwise in .../dplr/naive.py:41-101). tf32 operands keep the result
 // within 2e-3 of the fp32 recurrence after 4096 tokens; bf16 operands do not.
-#include "tcgen05.cuh"
+#include "chunk_common.cuh"
 
 namespace wkvm {
 namespace {
@@ -433,96 +433,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     // copies overlap the rest of this one.
     if (c + 1 < nchunks) stage(c + 1);
 
-    // ---- T = (I - A_ab)^-1 (unit lower triangular), blocked 16 -> 32 -> 64,
-    //      row-major in the G region, then as a K-major tile (row t', K = t).
-    {
-      float* Tr = Grow;
-      if (tid < 64) {  // diagonal 16 x 16 blocks, one column per thread
-        const int col = tid, b0 = col & ~15, ci = col & 15;
-        float y[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v = (i == ci) ? 1.f : 0.f;
-#pragma unroll
-          for (int i2 = 0; i2 < i; ++i2) v = fmaf(Aab[(b0 + i) * RS + b0 + i2], y[i2], v);
-          y[i] = (i < ci) ? 0.f : v;
-          Tr[(b0 + i) * RS + col] = y[i];
-        }
-      }
-      __syncthreads();
-      {  // blocks (1,0) and (3,2) of 16: X = A T_jj, then T_ij = T_ii X.
-         // Thread: row r = (tid >> 4) & 15, column cc = tid & 15 of both blocks.
-        const int r = (tid >> 4) & 15, cc = tid & 15;
-        float xv[2] = {0.f, 0.f};
-#pragma unroll
-        for (int s2 = 0; s2 < 16; ++s2) {
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const float tv = Tr[(32 * q + s2) * RS + 32 * q + cc];
-            const float av = Aab[(32 * q + 16 + r) * RS + 32 * q + s2];
-            xv[q] = fmaf(av, s2 >= cc ? tv : 0.f, xv[q]);
-          }
-        }
-        if (tid < 256) {
-#pragma unroll
-          for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[q];
-        }
-        __syncthreads();
-        float yv[2] = {0.f, 0.f};
-#pragma unroll
-        for (int s2 = 0; s2 < 16; ++s2) {
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const float tv = Tr[(32 * q + 16 + r) * RS + 32 * q + 16 + s2];
-            const float xx = Tr[(32 * q + 16 + s2) * RS + 32 * q + cc];
-            yv[q] = fmaf(s2 <= r ? tv : 0.f, xx, yv[q]);
-          }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = yv[q];
-      }
-      __syncthreads();
-      {  // block (1,0) of 32: X = A T_00, then T_10 = T_11 X. Thread: column
-         // C = tid & 31, rows 32 + (tid >> 5) + 8 q.
-        const int C = tid & 31, r0 = tid >> 5;
-        float xv[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int s2 = 0; s2 < 32; ++s2) {
-          const float tv = s2 >= C ? Tr[s2 * RS + C] : 0.f;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) xv[q] = fmaf(Aab[(32 + r0 + 8 * q) * RS + s2], tv, xv[q]);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = xv[q];
-        __syncthreads();
-        float yv[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int s2 = 0; s2 < 32; ++s2) {
-          const float xx = Tr[(32 + s2) * RS + C];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int R = r0 + 8 * q;
-            yv[q] = fmaf(s2 <= R ? Tr[(32 + R) * RS + 32 + s2] : 0.f, xx, yv[q]);
-          }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = yv[q];
-      }
-      __syncthreads();
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {  // K-major tile, zero above the diagonal;
-        // lanes walk 8 rows x 4 K-quads so each store instruction fills 512
-        // contiguous bytes
-        const int e = tid + 256 * q;
-        const int tp = (e >> 7) * 8 + (e & 7), t4 = ((e >> 3) & 15) * 4;
-        float v4[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v4[i] = (t4 + i <= tp) ? Tr[tp * RS + t4 + i] : 0.f;
-        kst4(sm + S_TT, tp, t4, make_float4(v4[0], v4[1], v4[2], v4[3]));
-      }
-    }
+    // ---- T = (I - A_ab)^-1 as a K-major tile (row t', K = t); G is spent
+    chunkc::tri_inverse64(Aab, Grow, sm + S_TT, tid);
     sync_tc();
 
     // ---- MMA S: [(A_ak V)^T; (a e^Gx)^T] x T^T -> T_D3 = [U~^T; W^T]

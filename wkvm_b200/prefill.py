@@ -1,10 +1,10 @@
 """Prefill entry points (chunk_rwkv7 / chunk_gated_delta_rule and their
 slot-native forms).
 
-RWKV-7 (head dim 64) runs the fused chunked tensor-core kernel
-(wkvm_chunk_dplr / wkvm_wkv7_prefill_slots: tcgen05 tf32, 64-token chunks,
-state kept on chip across chunks). Other head sizes and the GDN sibling run
-the recurrent kernel, which streams the state once and loops over tokens.
+RWKV-7 (head dim 64) and the GDN sibling (K = V = 128) run fused chunked
+tensor-core kernels (tcgen05 tf32, 64-token chunks, state kept on chip
+across chunks). Other head sizes run the recurrent kernel, which streams the
+state once and loops over tokens.
 The initial state comes from ``initial_state`` (or a bank slot) and the final
 state goes to a new tensor (or back into the slot).
 """
@@ -25,10 +25,23 @@ def chunk_dplr(r, w, k, v, a, b, scale, initial_state, output_final_state, cu_se
 
 def chunk_gdn(q, k, v, g, beta, scale, initial_state, output_final_state, use_qk_l2norm,
               cu_seqlens):
-    return _ops.fused_recurrent_gated_delta_rule(
-        q, k, v, g=g, beta=beta, scale=scale, initial_state=initial_state,
-        output_final_state=output_final_state, use_qk_l2norm_in_kernel=use_qk_l2norm,
-        cu_seqlens=cu_seqlens)
+    """fla chunk_gated_delta_rule semantics; returns (o, final_state or None)."""
+    _ops._require_cuda(q, k, v, g, beta, initial_state)
+    (q, k, v, g, beta), dt = _ops._acts(q, k, v, g, beta)
+    B, T, H, K = q.shape
+    HV, V = v.shape[2], v.shape[3]
+    N = B if cu_seqlens is None else len(cu_seqlens) - 1
+    cu = _ops._cu(cu_seqlens, q.device)
+    h0 = _ops._state(initial_state)
+    o = torch.empty_like(v)
+    ht = torch.empty(N, HV, K, V, dtype=torch.float32, device=q.device) if output_final_state else None
+    with torch.cuda.device(q.device):
+        _lib.call("wkvm_chunk_gated_delta_rule", _ops._ptr(q), _ops._ptr(k), _ops._ptr(v),
+                  _ops._ptr(g), _ops._ptr(beta), _ops._ptr(o), _ops._ptr(h0), _ops._ptr(ht),
+                  _ops._ptr(cu), N if cu is not None else B, T, H, HV, K, V, float(scale),
+                  int(bool(use_qk_l2norm)), dt, _ops._ptr(_ops.status_word(q.device)),
+                  _ops._stream(q.device))
+    return o, ht
 
 
 def wkv7_prefill_slots(r, w, k, v, kk, a, bank_wkv, layer, slot_ids, cu_seqlens=None,
@@ -58,8 +71,26 @@ def wkv7_prefill_slots(r, w, k, v, kk, a, bank_wkv, layer, slot_ids, cu_seqlens=
 
 
 def gdn_prefill_slots(q, k, v, g, beta, bank, layer, slot_ids, scale, use_qk_l2norm,
-                      cu_seqlens=None):
-    if cu_seqlens is not None:
-        raise NotImplementedError("varlen GDN slot prefill: pass one row per sequence")
-    return _ops.gdn_decode_slots(q, k, v, g, beta, bank, layer, slot_ids, scale,
-                                 use_qk_l2norm)
+                      cu_seqlens=None, out=None):
+    """Chunked GDN prefill with initial and final state in bank[layer, slot_ids]."""
+    _ops._require_cuda(q, k, v, g, beta, bank)
+    layer_t = _ops._bank_layer(bank, layer)
+    (q, k, v, g, beta), dt = _ops._acts(q, k, v, g, beta)
+    B, T, H, K = q.shape
+    HV, V = v.shape[2], v.shape[3]
+    if tuple(layer_t.shape[1:]) != (HV, K, V):
+        raise ValueError("bank layer shape does not match HV, K, V")
+    _ops._check_varlen(q, None, cu_seqlens)
+    nseq = B if cu_seqlens is None else len(cu_seqlens) - 1
+    ids = _ops.slot_ids_tensor(slot_ids, layer_t.shape[0], q.device)
+    if ids.numel() != nseq:
+        raise ValueError(f"{ids.numel()} slot ids for {nseq} sequences")
+    cu = _ops._cu(cu_seqlens, q.device)
+    o = torch.empty_like(v) if out is None else out
+    with torch.cuda.device(q.device):
+        _lib.call("wkvm_gdn_prefill_slots", _ops._ptr(q), _ops._ptr(k), _ops._ptr(v),
+                  _ops._ptr(g), _ops._ptr(beta), _ops._ptr(o), _ops._ptr(layer_t),
+                  layer_t.shape[0], _ops._ptr(ids), _ops._ptr(cu), nseq, T, H, HV, K, V,
+                  float(scale), int(bool(use_qk_l2norm)), dt,
+                  _ops._ptr(_ops.status_word(q.device)), _ops._stream(q.device))
+    return o
