@@ -372,6 +372,80 @@ def run_prefill(args, world, rank, local):
     }
 
 
+def run_gdn(args, world, rank, local):
+    """BASELINE config 3, gated delta rule (H=16, K=V=128): decode of B=512
+    slots in place in a 513-slot arena (--workload gdn-decode), or chunked
+    prefill of B=4 x 8192 tokens into slots (--workload gdn-prefill)."""
+    from wkvm_b200 import ops, synth
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    decode = args.workload == "gdn-decode"
+    B, T, HG, K = (512, 1, 16, 128) if decode else (4, 8192, 16, 128)
+    bank = torch.empty(1, B + 1, HG, K, K, device=dev)
+    bank.normal_(0.0, 0.1, generator=torch.Generator(device=dev).manual_seed(11 + rank))
+    ids = ops.slot_ids_tensor(list(range(1, B + 1)), B + 1, dev)
+    x = synth.gdn_inputs(B, T, HG, K, seed=rank, device=dev, state=False)
+    o = torch.empty_like(x["v"])
+    ops.status_word(dev)
+
+    def step():
+        if decode:
+            ops.gdn_decode_slots(x["q"], x["k"], x["v"], x["g"], x["beta"], bank, 0, ids, out=o)
+        else:
+            from wkvm_b200 import prefill
+            prefill.gdn_prefill_slots(x["q"], x["k"], x["v"], x["g"], x["beta"], bank, 0, ids,
+                                      K ** -0.5, False, out=o)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index if dev.index is not None else 0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        stop.record()
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world, dev)
+    ops.check_device_status(dev)
+    if rank != 0:
+        return None
+    step_ms = ms / args.steps
+    hbm_peak, kind = peaks()
+    th = B * T * HG  # token-heads
+    if decode:
+        byts = B * HG * 132100          # state r+w 128 KiB + q,k,v,g,beta + o per slot-head
+        line_roof = {"bound": "hbm", "achieved": round(byts / (step_ms * 1e-3) / 1e9, 1),
+                     "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(byts / (step_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                     "peak_kind": f"{kind} hbm_gbs", "bytes_per_launch": byts}
+        kernel = "gdn_recurrent_kernel<128,128,16> (gdn_decode_slots)"
+    else:
+        byts = th * 1028 + 2 * B * HG * K * K * 4
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        line_roof = {"bound": "hbm", "achieved": round(byts / (step_ms * 1e-3) / 1e9, 1),
+                     "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(byts / (step_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                     "tensor_tflops": round(th * 183e3 / (step_ms * 1e-3) / 1e12, 2),
+                     "tensor_peak_tflops": d.get("bf16_tflops", 1590.0) / 2,
+                     "tensor_peak_kind": "measured bf16_tflops / 2 (tf32 dense rate)"}
+        kernel = "gdn_chunk_kernel (tcgen05 kind::tf32)"
+    return {
+        "metric": f"GDN {'decode' if decode else 'chunked prefill'} tokens/s (BASELINE config 3)",
+        "value": round(world * B * T * args.steps / (ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 in/out, fp32 state",
+        "data": "synthetic (seeded, reference op-level distributions)",
+        "config": {"workload": f"B={B} T={T} H=16 K=V=128, state in arena slots",
+                   "kernel": kernel},
+        "roofline": line_roof, "clocks": clk.summary(), "gpu_launches": args.steps,
+    }
+
+
 def _cpu_sample(slots: int, threads: int, seed: int = 0):
     """One decode token through all 24 layers for ``slots`` slots with the
     fp32 oracle; returns seconds."""
@@ -441,7 +515,8 @@ def main():
                     help="plain launches instead of programmatic dependent launch")
     ap.add_argument("--layers", type=int, default=24,
                     help="layers per decode step (24 = the benchmark; fewer for profiling)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "gdn-decode", "gdn-prefill"])
     ap.add_argument("--prefill-batch", type=int, default=16)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -456,6 +531,8 @@ def main():
         world, rank, local = dist_setup()
         if args.workload == "prefill":
             line = run_prefill(args, world, rank, local)
+        elif args.workload.startswith("gdn"):
+            line = run_gdn(args, world, rank, local)
         else:
             line = run_ours(args, world, rank, local)
         if world > 1:
