@@ -446,6 +446,137 @@ def run_gdn(args, world, rank, local):
     }
 
 
+def run_model_decode(args, world, rank, local):
+    """BASELINE config 1 as a whole decode step: fla's RWKV-7 model (the model
+    wkvm serves) at the 1.5B shape (L=24, D=2048, H=32, vocab 65536, random
+    bf16 weights, std 0.02), 256 active slots of a 1024-slot arena. Two arms
+    on the same box and weights:
+      ours      - fla model with wkvm_b200's ops installed, WKV state read and
+                  written in the arena by slot id (fla_compat.slot_cache);
+      reference - wkvm's gather -> fla model with fla's Triton ops -> scatter
+                  (per-layer index_select / index_copy_, as
+                  wkvm/runner/state.py:63-97 does)."""
+    from fla.models.rwkv7 import RWKV7Config, RWKV7ForCausalLM
+    from fla.models.utils import Cache
+    from wkvm_b200 import fla_compat, ops, synth
+    from wkvm_b200.state import RWKV7StateBank, RWKV7StateLayout
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.manual_seed(rank)
+    cfg = RWKV7Config(hidden_size=H * N, num_hidden_layers=L, head_dim=N, vocab_size=65536)
+    with torch.device(dev):
+        model = RWKV7ForCausalLM(cfg)
+    model = model.to(torch.bfloat16).eval().requires_grad_(False)
+    layout = RWKV7StateLayout(n_layer=L, hidden_size=H * N, num_heads=H, head_dim=N,
+                              head_v_dim=N, dtype=torch.bfloat16)
+    bank = RWKV7StateBank(layout, NUM_SLOTS, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+    bank.wkv.normal_(0.0, 0.1, generator=gen)
+    bank.shift.normal_(0.0, 0.5, generator=gen)
+    ids_host = synth.slot_ids(ACTIVE, NUM_SLOTS + 1, seed=rank).tolist()
+    ids_dev = torch.tensor(ids_host, dtype=torch.int32, device=dev)
+    ids_long = ids_dev.long()
+    tokens = torch.randint(0, 65536, (ACTIVE, 1), device=dev, generator=gen)
+
+    def ref_step():
+        cache = Cache()
+        for i in range(L):
+            cache.update(recurrent_state=bank.wkv[i].index_select(0, ids_long),
+                         conv_state=bank.shift[i, 0].index_select(0, ids_long),
+                         ffn_state=bank.shift[i, 1].index_select(0, ids_long),
+                         layer_idx=i, offset=0)
+        out = model(input_ids=tokens, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        for i in range(L):
+            st = cache[i]
+            bank.wkv[i].index_copy_(0, ids_long, st["recurrent_state"].float())
+            bank.shift[i, 0].index_copy_(0, ids_long, st["conv_state"])
+            bank.shift[i, 1].index_copy_(0, ids_long, st["ffn_state"])
+        return out.logits
+
+    def our_step():
+        h = fla_compat.slot_cache(bank, ids_dev)
+        out = model(input_ids=tokens, past_key_values=h.cache, use_cache=True, logits_to_keep=1)
+        h.commit()
+        return out.logits
+
+    def timed(step):
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            step()
+        s1.record()
+        torch.cuda.synchronize(dev)
+        return s0.elapsed_time(s1) / args.steps
+
+    with torch.inference_mode():
+        # parity: one step of each arm from the same state
+        w0, sh0 = bank.wkv.clone(), bank.shift.clone()
+        fla_compat.uninstall()
+        ref_logits = ref_step().float()
+        ref_state = bank.wkv[:, ids_long].clone()
+        bank.wkv.copy_(w0)
+        bank.shift.copy_(sh0)
+        fla_compat.install()
+        our_logits = our_step().float()
+        our_state = bank.wkv[:, ids_long].clone()
+        parity = {
+            "logits_max_rel": float((our_logits - ref_logits).abs().max() / ref_logits.abs().max()),
+            "argmax_agree": float((our_logits.argmax(-1) == ref_logits.argmax(-1)).float().mean()),
+            "state_max_rel": float((our_state - ref_state).abs().max() / ref_state.abs().max()),
+        }
+        del w0, sh0
+
+        def graphed(step):
+            """Whole decode step captured once as a CUDA graph, then replayed
+            (the reference's engine bench graphs its decode step too)."""
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                for _ in range(2):
+                    step()
+            torch.cuda.current_stream(dev).wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step()
+            return g.replay
+
+        clk_ctx = Clocks(dev.index if dev.index is not None else 0)
+        with clk_ctx as clk:
+            ours_ms = timed(graphed(our_step))
+        ours_eager_ms = timed(our_step)
+        fla_compat.uninstall()
+        ref_ms = timed(graphed(ref_step))
+        ref_eager_ms = timed(ref_step)
+    ops.check_device_status(dev)
+    ours_ms = max_over_ranks(ours_ms, world, dev)
+    ref_ms = max_over_ranks(ref_ms, world, dev)
+    if rank != 0:
+        return None
+    return {
+        "metric": "RWKV-7 1.5B-shape full decode step tokens/s (BASELINE config 1)",
+        "value": round(world * ACTIVE / (ours_ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ours_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 weights and activations, fp32 WKV state",
+        "data": "synthetic (random-init weights std 0.02, random tokens and states)",
+        "config": {"workload": "fla RWKV7ForCausalLM L=24 D=2048 H=32 vocab 65536, 256 active "
+                               "of 1024 arena slots, whole step as one CUDA graph, "
+                               "logits_to_keep=1",
+                   "global_batch": ACTIVE * world},
+        "eager_ms_per_step": round(ours_eager_ms, 4),
+        "same_box_reference": {"ms_per_step": round(ref_ms, 4),
+                               "value": round(world * ACTIVE / (ref_ms * 1e-3), 1),
+                               "eager_ms_per_step": round(ref_eager_ms, 4),
+                               "path": "gather -> fla Triton ops -> scatter (wkvm's runner flow)"},
+        "parity_one_step": parity,
+        "clocks": clk.summary(),
+    }
+
+
 def _cpu_sample(slots: int, threads: int, seed: int = 0):
     """One decode token through all 24 layers for ``slots`` slots with the
     fp32 oracle; returns seconds."""
@@ -516,7 +647,7 @@ def main():
     ap.add_argument("--layers", type=int, default=24,
                     help="layers per decode step (24 = the benchmark; fewer for profiling)")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "gdn-decode", "gdn-prefill"])
+                    choices=["decode", "prefill", "gdn-decode", "gdn-prefill", "model-decode"])
     ap.add_argument("--prefill-batch", type=int, default=16)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -531,6 +662,8 @@ def main():
         world, rank, local = dist_setup()
         if args.workload == "prefill":
             line = run_prefill(args, world, rank, local)
+        elif args.workload == "model-decode":
+            line = run_model_decode(args, world, rank, local)
         elif args.workload.startswith("gdn"):
             line = run_gdn(args, world, rank, local)
         else:

@@ -179,6 +179,18 @@ int wkvm_wkv7_prefill_slots(
     int32_t B, int32_t T, int32_t H, int32_t K, int32_t V,
     int32_t dtype, int32_t* status, wkvm_stream_t stream);
 
+/* Slot-native prefill in fla's general DPLR form (explicit a, b and scale),
+ * the arguments fla's RWKV7Attention passes to chunk_rwkv7
+ * (fla/layers/rwkv7.py:308-321). Head dim 64 with 16-bit inputs only
+ * (WKVM_ERR_UNSUPPORTED otherwise). */
+int wkvm_dplr_prefill_slots(
+    const void* r, const void* w, const void* k, const void* v,
+    const void* a, const void* b, void* o,
+    float* bank_layer, int64_t num_slots, const int32_t* slot_ids,
+    const int64_t* cu_seqlens,
+    int32_t B, int32_t T, int32_t H, int32_t K, int32_t V,
+    float scale, int32_t dtype, int32_t* status, wkvm_stream_t stream);
+
 /* Chunked GDN prefill: replaces fla `chunk_gated_delta_rule`
  * (fla/ops/gated_delta_rule/chunk.py:365, forward :29-116) for head-wise g
  * and beta, [K,V] state layout. Arguments as for

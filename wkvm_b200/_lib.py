@@ -38,6 +38,7 @@ SIGNATURES: dict[str, list] = {
     "wkvm_selftest_tf32_mma": [P, P, P, I32, I32, P, P],
     "wkvm_chunk_dplr": [P] * 7 + [P, P, P] + [I32] * 5 + [F32, I32, P, P],
     "wkvm_wkv7_prefill_slots": [P] * 7 + [P, I64, P, P] + [I32] * 5 + [I32, P, P],
+    "wkvm_dplr_prefill_slots": [P] * 7 + [P, I64, P, P] + [I32] * 5 + [F32, I32, P, P],
     "wkvm_chunk_gated_delta_rule": [P] * 6 + [P, P, P] + [I32] * 6 + [F32, I32, I32, P, P],
     "wkvm_gdn_prefill_slots": [P] * 6 + [P, I64, P, P] + [I32] * 6 + [F32, I32, I32, P, P],
 }

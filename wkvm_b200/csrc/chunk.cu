@@ -619,3 +619,22 @@ extern "C" int wkvm_wkv7_prefill_slots(const void* r, const void* w, const void*
     return wkvm::launch_chunk_t<__nv_bfloat16, true>(args, B * H, (cudaStream_t)stream);
   return wkvm::launch_chunk_t<__half, true>(args, B * H, (cudaStream_t)stream);
 }
+
+extern "C" int wkvm_dplr_prefill_slots(const void* r, const void* w, const void* k, const void* v,
+                                       const void* a, const void* b, void* o, float* bank_layer,
+                                       int64_t num_slots, const int32_t* slot_ids,
+                                       const int64_t* cu_seqlens, int32_t B, int32_t T, int32_t H,
+                                       int32_t K, int32_t V, float scale, int32_t dtype,
+                                       int32_t* status, wkvm_stream_t stream) {
+  if (!bank_layer || num_slots <= 0 || (B > 0 && !slot_ids)) return WKVM_ERR_INVALID_ARG;
+  const void* ptrs[7] = {r, w, k, v, a, b, o};
+  if (!chunk_path_ok(K, V, dtype, ptrs, 7)) return WKVM_ERR_UNSUPPORTED;
+  if (B < 0 || T < 0 || H <= 0) return WKVM_ERR_INVALID_ARG;
+  if (B == 0) return WKVM_OK;
+  if (!wkvm::al16(bank_layer)) return WKVM_ERR_ALIGN;
+  wkvm::ChunkArgs args{r, w, k, v, a, b, o, bank_layer, bank_layer, slot_ids, num_slots,
+                       cu_seqlens, T, H, scale, status};
+  if (dtype == WKVM_DTYPE_BF16)
+    return wkvm::launch_chunk_t<__nv_bfloat16, false>(args, B * H, (cudaStream_t)stream);
+  return wkvm::launch_chunk_t<__half, false>(args, B * H, (cudaStream_t)stream);
+}

@@ -51,7 +51,10 @@ def status_word(device: torch.device | int | str | None = None) -> torch.Tensor:
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     t = _status.get(idx)
     if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        # a normal tensor even when first requested under inference_mode, so
+        # it can be reset anywhere
+        with torch.inference_mode(False):
+            t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
         _status[idx] = t
     return t
 
