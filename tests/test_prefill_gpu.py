@@ -173,3 +173,22 @@ def test_gdn_prefill_slots_varlen(cuda):
     assert rel_err(bank[0, ids], rh) < REL_TOL
     rest = [0, 1, 3]
     assert torch.equal(bank[0, rest], before[0, rest]) and torch.equal(bank[0, 2], before[0, 2])
+
+
+def test_chunk_rwkv7_varlen_cu_seqlens(cuda):
+    lens = [130, 0, 64, 7]
+    H, N = 2, 64
+    x = synth.rwkv7_inputs(1, sum(lens), H, N, seed=41, num_states=len(lens))
+    d = _to(x, cuda)
+    a, b = _ab(d)
+    cu = torch.tensor(np.cumsum([0] + lens), dtype=torch.int64)
+    o, ht = ops.chunk_rwkv7(d["r"], d["w"], d["k"], d["v"], a, b, scale=1.0,
+                            initial_state=d["h0"], output_final_state=True,
+                            cu_seqlens=cu.to(cuda))
+    ro, rh = oracle.dplr_recurrence(np32(d["r"]), np32(d["w"]), np32(d["k"]), np32(d["v"]),
+                                    np32(a), np32(b), initial_state=np32(x["h0"]),
+                                    cu_seqlens=cu.numpy())
+    ops.check_device_status(cuda)
+    assert_out_close(o, ro)
+    assert rel_err(ht, rh) < REL_TOL
+    assert torch.equal(ht[1], d["h0"][1])
