@@ -257,6 +257,21 @@ int wkvm_slot_restore(void* base, int64_t outer, int64_t outer_stride,
                       const void* packed, int32_t* status,
                       wkvm_stream_t stream);
 
+/* Gather / scatter with an explicit layout of the packed side: element
+ * (outer o, batch index i) of the packed buffer starts at
+ * o * dst_outer_stride + i * dst_index_stride bytes (snapshot/restore are the
+ * case dst_index_stride = outer * row_bytes). Used to hand a model one
+ * contiguous [n, row] view per layer of a family (the reference gathers with
+ * one index_select per layer and family, wkvm/runner/state.py:76-79). */
+int wkvm_slot_gather(const void* base, int64_t outer, int64_t outer_stride,
+                     int64_t slot_stride, int64_t row_bytes, int64_t num_slots,
+                     const int32_t* ids, int32_t n, void* dst, int64_t dst_outer_stride,
+                     int64_t dst_index_stride, int32_t* status, wkvm_stream_t stream);
+int wkvm_slot_scatter(void* base, int64_t outer, int64_t outer_stride,
+                      int64_t slot_stride, int64_t row_bytes, int64_t num_slots,
+                      const int32_t* ids, int32_t n, const void* src, int64_t src_outer_stride,
+                      int64_t src_index_stride, int32_t* status, wkvm_stream_t stream);
+
 /* Live migration: rows of dst_ids[i] in dst_base (a peer GPU's bank, peer
  * access enabled by the caller) <- rows of src_ids[i] in src_base. Both
  * banks share outer/strides/row size. Plain peer stores over NVLink; launch

@@ -31,6 +31,8 @@ SIGNATURES: dict[str, list] = {
     "wkvm_slot_zero": [P, I64, I64, I64, I64, I64, P, I32, P, P],
     "wkvm_slot_snapshot": [P, I64, I64, I64, I64, I64, P, I32, P, P, P],
     "wkvm_slot_restore": [P, I64, I64, I64, I64, I64, P, I32, P, P, P],
+    "wkvm_slot_gather": [P, I64, I64, I64, I64, I64, P, I32, P, I64, I64, P, P],
+    "wkvm_slot_scatter": [P, I64, I64, I64, I64, I64, P, I32, P, I64, I64, P, P],
     "wkvm_slot_migrate": [P, P, I64, I64, I64, I64, I64, I64, P, P, I32, P, P],
     "wkvm_enable_peer_access": [I32, I32],
     "wkvm_set_decode_overlap": [I32],

@@ -192,6 +192,28 @@ extern "C" int wkvm_slot_restore(void* base, int64_t outer, int64_t outer_stride
   return wkvm::launch_move(a, n, (cudaStream_t)stream);
 }
 
+extern "C" int wkvm_slot_gather(const void* base, int64_t outer, int64_t outer_stride,
+                                int64_t slot_stride, int64_t row_bytes, int64_t num_slots,
+                                const int32_t* ids, int32_t n, void* dst,
+                                int64_t dst_outer_stride, int64_t dst_index_stride,
+                                int32_t* status, wkvm_stream_t stream) {
+  if (!base || !dst || (n > 0 && !ids)) return WKVM_ERR_INVALID_ARG;
+  MoveArgs a{(const char*)base, (char*)dst, outer_stride, slot_stride, dst_outer_stride,
+             dst_index_stride, row_bytes, outer, ids, nullptr, num_slots, (int64_t)n, 0, status};
+  return wkvm::launch_move(a, n, (cudaStream_t)stream);
+}
+
+extern "C" int wkvm_slot_scatter(void* base, int64_t outer, int64_t outer_stride,
+                                 int64_t slot_stride, int64_t row_bytes, int64_t num_slots,
+                                 const int32_t* ids, int32_t n, const void* src,
+                                 int64_t src_outer_stride, int64_t src_index_stride,
+                                 int32_t* status, wkvm_stream_t stream) {
+  if (!base || !src || (n > 0 && !ids)) return WKVM_ERR_INVALID_ARG;
+  MoveArgs a{(const char*)src, (char*)base, src_outer_stride, src_index_stride, outer_stride,
+             slot_stride, row_bytes, outer, nullptr, ids, (int64_t)n, num_slots, 0, status};
+  return wkvm::launch_move(a, n, (cudaStream_t)stream);
+}
+
 extern "C" int wkvm_slot_migrate(const void* src_base, void* dst_base, int64_t outer,
                                  int64_t outer_stride, int64_t slot_stride, int64_t row_bytes,
                                  int64_t src_num_slots, int64_t dst_num_slots,

@@ -109,24 +109,25 @@ class SlotCacheHandle:
         dev = bank.device
         self.ids = ops.slot_ids_tensor(slot_ids, bank.num_slots + 1, dev)
         L = bank.layout.n_layer
-        self.shift = ops.slot_snapshot(bank.shift, 2, self.ids,
-                                       out=torch.empty((self.ids.numel(), L, 2,
-                                                        bank.layout.hidden_size),
-                                                       dtype=bank.shift.dtype, device=dev))
+        # [L, 2, n, D]: one kernel, and every (layer, family) view is contiguous
+        self.shift = ops.slot_gather_outer_major(bank.shift, 2, self.ids)
         self.cache = Cache()
         for i in range(L):
             self.cache.update(recurrent_state=SlotState(bank.wkv, i, self.ids),
-                              conv_state=self.shift[:, i, 0].contiguous(),
-                              ffn_state=self.shift[:, i, 1].contiguous(),
+                              conv_state=self.shift[i, 0], ffn_state=self.shift[i, 1],
                               layer_idx=i, offset=0)
 
     def commit(self) -> None:
+        """Writes each layer's new token-shift rows back to the bank."""
         L = self.bank.layout.n_layer
         for i in range(L):
             st = self.cache[i]
-            self.shift[:, i, 0].copy_(st["conv_state"])
-            self.shift[:, i, 1].copy_(st["ffn_state"])
-        ops.slot_restore(self.bank.shift, 2, self.ids, self.shift)
+            for j, key in ((0, "conv_state"), (1, "ffn_state")):
+                x = st[key]
+                if x.data_ptr() == self.shift[i, j].data_ptr():
+                    x = self.shift[i, j]
+                ops.slot_restore(self.bank.shift[i, j], 0, self.ids,
+                                 x.reshape(self.ids.numel(), -1).to(self.bank.shift.dtype))
 
 
 def slot_cache(bank, slot_ids) -> SlotCacheHandle:

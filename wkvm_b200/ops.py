@@ -499,3 +499,22 @@ def slot_affine(family: torch.Tensor, slot_dim: int, dst_ids, a_ids, b_ids, c1: 
         _lib.call("wkvm_slot_affine", _ptr(family), outer, ostr, sstr, row, ns, _ptr(d),
                   _ptr(a), _ptr(b), d.numel(), float(c1), float(c2), dt,
                   _ptr(status_word(family.device)), _stream(family.device))
+
+
+def slot_gather_outer_major(family: torch.Tensor, slot_dim: int, ids,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Gathers the rows of ``ids`` into ``out`` [*outer_shape, n, *row_shape]:
+    for every outer index a contiguous [n, row] block (one kernel)."""
+    outer, ostr, sstr, row, ns = _family_geometry(family, slot_dim)
+    i = slot_ids_tensor(ids, ns, family.device)
+    n = i.numel()
+    shape = (*family.shape[:slot_dim], n, *family.shape[slot_dim + 1:])
+    if out is None:
+        out = torch.empty(shape, dtype=family.dtype, device=family.device)
+    if tuple(out.shape) != shape or not out.is_contiguous():
+        raise ValueError(f"gather buffer must be contiguous {shape}")
+    with torch.cuda.device(family.device):
+        _lib.call("wkvm_slot_gather", _ptr(family), outer, ostr, sstr, row, ns, _ptr(i), n,
+                  _ptr(out), n * row, row, _ptr(status_word(family.device)),
+                  _stream(family.device))
+    return out
