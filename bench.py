@@ -551,6 +551,15 @@ def run_model_decode(args, world, rank, local):
         with clk_ctx as clk:
             ours_ms = timed(graphed(our_step))
         ours_eager_ms = timed(our_step)
+        # the same with the time-mix core fused around the WKV step
+        fla_compat.install(fuse_time_mix=True)
+        w1, sh1 = bank.wkv.clone(), bank.shift.clone()
+        fused_logits = our_step().float()
+        bank.wkv.copy_(w1)
+        bank.shift.copy_(sh1)
+        del w1, sh1
+        fused_ms = timed(graphed(our_step))
+        fla_compat.install(fuse_time_mix=False)
         fla_compat.uninstall()
         ref_ms = timed(graphed(ref_step))
         ref_eager_ms = timed(ref_step)
@@ -571,6 +580,9 @@ def run_model_decode(args, world, rank, local):
                                "logits_to_keep=1",
                    "global_batch": ACTIVE * world},
         "eager_ms_per_step": round(ours_eager_ms, 4),
+        "fused_time_mix": {"ms_per_step": round(fused_ms, 4),
+                           "value": round(world * ACTIVE / (fused_ms * 1e-3), 1),
+                           "note": "gates, norms and output correction inside the decode kernel"},
         "same_box_reference": {"ms_per_step": round(ref_ms, 4),
                                "value": round(world * ACTIVE / (ref_ms * 1e-3), 1),
                                "eager_ms_per_step": round(ref_eager_ms, 4),

@@ -116,6 +116,23 @@ int wkvm_wkv7_decode_slots(
  * No counterpart in the reference. */
 int wkvm_set_decode_overlap(int32_t enable);
 
+/* Fused RWKV-7 time-mix decode core: the whole of fla RWKV7Attention between
+ * its projections and o_proj for one token, around an in-place slot update
+ * (fla/layers/rwkv7.py:270-349): w = -0.6065306597126334 sigmoid(w_raw),
+ * a = sigmoid(a_raw), v = lerp(v, v_first, sigmoid(v_raw)) (v_first and
+ * v_raw NULL for layer 0), kk = l2norm(k k_k) per head, k' = k + k (a-1) k_a,
+ * the WKV step on bank_layer[slot_ids[i]], then GroupNorm per head
+ * (gn_w, gn_b, gn_eps), o += (sum r k' r_k) v, o *= g. Activations are
+ * [B, H*64] rows; k_k, k_a, r_k, gn_w, gn_b are [H*64] parameters in the
+ * same dtype. Head dim 64. */
+int wkvm_wkv7_timemix_decode_slots(
+    const void* r, const void* w_raw, const void* k, const void* v,
+    const void* v_first, const void* v_raw, const void* a_raw, const void* g,
+    const void* k_k, const void* k_a, const void* r_k, const void* gn_w,
+    const void* gn_b, void* o, float* bank_layer, int64_t num_slots,
+    const int32_t* slot_ids, int32_t B, int32_t H, int32_t K, float gn_eps,
+    int32_t dtype, int32_t* status, wkvm_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Gated delta rule (GDN) recurrent form.
  *

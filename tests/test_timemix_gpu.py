@@ -1,0 +1,119 @@
+"""Fused RWKV-7 time-mix decode core against the same chain of fla's
+formulas (fla/layers/rwkv7.py:270-349) computed step by step in fp32."""
+
+import pytest
+import torch
+
+from conftest import REL_TOL, assert_out_close, rel_err
+from wkvm_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _reference_chain(r, w_raw, k, v, v_first, v_raw, a_raw, g, k_k, k_a, r_k, gn_w, gn_b, eps,
+                     h0):
+    B, D = r.shape
+    H, N = D // 64, 64
+    f = lambda t: t.float()
+    w = -0.6065306597126334 * torch.sigmoid(f(w_raw))
+    vv = f(v)
+    if v_first is not None:
+        vv = torch.lerp(vv, f(v_first), torch.sigmoid(f(v_raw)))
+    a = torch.sigmoid(f(a_raw))
+    kk = (f(k) * f(k_k)).view(B, H, N)
+    kk = (kk / torch.sqrt((kk * kk).sum(-1, keepdim=True) + 1e-6)).view(B, D)
+    ku = f(k) + f(k) * (a - 1) * f(k_a)
+    sh = lambda t: t.view(B, 1, H, N).contiguous()
+    o, ht = ops.fused_mul_recurrent_rwkv7(sh(f(r)), sh(w), sh(ku), sh(vv), sh(kk), sh(a),
+                                          scale=1.0, initial_state=h0, output_final_state=True)
+    o = o.view(B, H, N)
+    mean = o.mean(-1, keepdim=True)
+    var = ((o - mean) ** 2).mean(-1, keepdim=True)
+    on = ((o - mean) / torch.sqrt(var + eps)).view(B, D) * f(gn_w) + f(gn_b)
+    corr = (f(r) * ku * f(r_k).view(D)).view(B, H, N).sum(-1, keepdim=True)
+    out = (on + (corr * vv.view(B, H, N)).view(B, D)) * f(g)
+    return out, ht
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("first_layer", [True, False])
+def test_timemix_matches_formula_chain(cuda, dtype, first_layer):
+    torch.manual_seed(0)
+    B, H, N, S = 6, 4, 64, 9
+    D = H * N
+    mk = lambda *s, sc=1.0: (torch.randn(*s, device=cuda) * sc).to(dtype)
+    r, w_raw, k, v, a_raw = mk(B, D), mk(B, D), mk(B, D), mk(B, D), mk(B, D)
+    g = torch.sigmoid(torch.randn(B, D, device=cuda)).to(dtype)
+    v_first = None if first_layer else mk(B, D)
+    v_raw = None if first_layer else mk(B, D)
+    k_k, k_a, r_k = mk(D, sc=0.5), mk(D, sc=0.5), mk(H, N, sc=0.5)
+    gn_w, gn_b = mk(D, sc=0.3), mk(D, sc=0.1)
+    eps = 64e-5
+    bank = (torch.randn(2, S, H, N, N, device=cuda) * 0.1)
+    ids = [7, 2, 5, 1, 8, 3]
+    h0 = bank[1, ids].clone()
+    ref, ht = _reference_chain(r, w_raw, k, v, v_first, v_raw, a_raw, g, k_k, k_a, r_k, gn_w,
+                               gn_b, eps, h0)
+    o = ops.wkv7_timemix_decode_slots(r, w_raw, k, v, v_first, v_raw, a_raw, g, k_k, k_a, r_k,
+                                      gn_w, gn_b, eps, bank, 1, ids)
+    ops.check_device_status(cuda)
+    assert rel_err(bank[1, ids], ht) < (1e-5 if dtype == torch.float32 else REL_TOL)
+    if dtype == torch.float32:
+        assert rel_err(o, ref) < 1e-4
+    else:
+        assert_out_close(o, ref)
+
+
+def test_fused_time_mix_model_decode_close_to_fla(cuda):
+    fla_models = pytest.importorskip("fla.models.rwkv7")
+    from fla.models.utils import Cache
+    from wkvm_b200 import fla_compat
+    from wkvm_b200.state import RWKV7StateBank, RWKV7StateLayout
+
+    torch.manual_seed(1)
+    L, D, N = 3, 256, 64
+    cfg = fla_models.RWKV7Config(hidden_size=D, num_hidden_layers=L, head_dim=N, vocab_size=512)
+    with torch.device(cuda):
+        model = fla_models.RWKV7ForCausalLM(cfg)
+    model = model.to(torch.bfloat16).eval()
+    for p in model.parameters():  # non-trivial parameters (fla's init zeroes some)
+        p.data.add_(torch.randn_like(p) * 0.05)
+    lay = RWKV7StateLayout(n_layer=L, hidden_size=D, num_heads=D // N, head_dim=N, head_v_dim=N)
+    ours = RWKV7StateBank(lay, num_slots=4, device=cuda)
+    ref = RWKV7StateBank(lay, num_slots=4, device=cuda)
+    for b in (ours, ref):
+        b.wkv.copy_(torch.randn_like(b.wkv, generator=torch.Generator(device=cuda).manual_seed(3)) * 0.1)
+    slots = [2, 4, 1]
+    ids = torch.tensor(slots, device=cuda)
+    tok = torch.randint(0, 512, (3, 1), device=cuda)
+
+    def ref_step(t):
+        cache = Cache()
+        for i in range(L):
+            cache.update(recurrent_state=ref.wkv[i].index_select(0, ids),
+                         conv_state=ref.shift[i, 0].index_select(0, ids),
+                         ffn_state=ref.shift[i, 1].index_select(0, ids), layer_idx=i, offset=0)
+        out = model(input_ids=t, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        for i in range(L):
+            ref.wkv[i].index_copy_(0, ids, cache[i]["recurrent_state"].float())
+            ref.shift[i, 0].index_copy_(0, ids, cache[i]["conv_state"])
+            ref.shift[i, 1].index_copy_(0, ids, cache[i]["ffn_state"])
+        return out.logits.float()
+
+    with torch.inference_mode():
+        fla_compat.uninstall()
+        ref_logits = [ref_step(tok) for _ in range(4)]
+        fla_compat.install(fuse_time_mix=True)
+        try:
+            our_logits = []
+            for _ in range(4):
+                h = fla_compat.slot_cache(ours, slots)
+                our_logits.append(model(input_ids=tok, past_key_values=h.cache, use_cache=True,
+                                        logits_to_keep=1).logits.float())
+                h.commit()
+        finally:
+            fla_compat.uninstall()
+    # fla rounds every intermediate to bf16; the fused core keeps fp32
+    for o, r in zip(our_logits, ref_logits):
+        assert rel_err(o, r) < 3e-2
+    assert rel_err(ours.wkv[:, slots], ref.wkv[:, slots]) < 3e-2

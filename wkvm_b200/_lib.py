@@ -25,6 +25,7 @@ SIGNATURES: dict[str, list] = {
     "wkvm_fused_mul_recurrent_rwkv7": [P] * 7 + [P, P, P] + [I32] * 5 + [F32, I32, P, P],
     "wkvm_fused_recurrent_dplr": [P] * 7 + [P, P, P] + [I32] * 5 + [F32, I32, P, P],
     "wkvm_wkv7_decode_slots": [P] * 7 + [P, I64, P] + [I32] * 5 + [I32, P, P],
+    "wkvm_wkv7_timemix_decode_slots": [P] * 14 + [P, I64, P, I32, I32, I32, F32, I32, P, P],
     "wkvm_fused_recurrent_gated_delta_rule": [P] * 6 + [P, P, P] + [I32] * 6 + [F32, I32, I32, P, P],
     "wkvm_gdn_decode_slots": [P] * 6 + [P, I64, P] + [I32] * 6 + [F32, I32, I32, P, P],
     "wkvm_slot_copy": [P, I64, I64, I64, I64, I64, P, P, I32, P, P],

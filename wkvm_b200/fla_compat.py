@@ -79,21 +79,66 @@ def chunk_rwkv7(r, w, k, v, a, b, scale: float = 1.0, initial_state=None,
                                cu_seqlens)
 
 
-def install() -> None:
-    """Points fla's RWKV7Attention at wkvm_b200's WKV ops (idempotent)."""
+def _fused_time_mix_forward(self, hidden_states, attention_mask=None, past_key_values=None,
+                            use_cache=False, output_attentions=False, v_first=None,
+                            cu_seqlens=None, **kwargs):
+    """RWKV7Attention.forward with the part between the projections and o_proj
+    in one kernel (wkv7_timemix_decode_slots), for single-token decode with
+    slot-resident state; every other case runs fla's own forward."""
+    import fla.layers.rwkv7 as layer
+    orig = _orig["forward"]
+    B, T, _ = hidden_states.shape
+    last = layer.get_layer_cache(self, past_key_values)
+    st = last["recurrent_state"] if last is not None else None
+    if (not isinstance(st, SlotState) or T != 1 or attention_mask is not None
+            or cu_seqlens is not None or self.training or not self.fuse_norm):
+        return orig(self, hidden_states, attention_mask, past_key_values, use_cache,
+                    output_attentions, v_first, cu_seqlens, **kwargs)
+    delta, conv_state = layer.token_shift(hidden_states, cu_seqlens, output_cache=True,
+                                          cache=last["conv_state"])
+    xr, xw, xk, xv, xa, xg = layer.fused_addcmul_rwkv7(hidden_states, delta, self.x_r, self.x_w,
+                                                       self.x_k, self.x_v, self.x_a, self.x_g)
+    r = self.r_proj(xr)
+    w_raw = self.w_lora(xw)
+    k = self.k_proj(xk)
+    v = self.v_proj(xv)
+    if self.layer_idx == 0:
+        v_first, vf, vr = v, None, None
+    else:
+        vf, vr = v_first, self.v_lora(xv)
+    a_raw = self.a_lora(xa)
+    g = self.g_lora(xg)
+    o = ops.wkv7_timemix_decode_slots(r, w_raw, k, v, vf, vr, a_raw, g, self.k_k, self.k_a,
+                                      self.r_k, self.g_norm.weight, self.g_norm.bias,
+                                      self.g_norm.eps, st.bank_wkv, st.layer, st.ids)
+    layer.update_layer_cache(self, past_key_values, recurrent_state=st, conv_state=conv_state,
+                             offset=T)
+    return self.o_proj(o), None, past_key_values, v_first
+
+
+def install(fuse_time_mix: bool = False) -> None:
+    """Points fla's RWKV7Attention at wkvm_b200's WKV ops (idempotent). With
+    ``fuse_time_mix`` single-token decode with slot-resident state also runs
+    the gates, norms and output correction inside the decode kernel."""
     import fla.layers.rwkv7 as layer
     if not _orig:
         _orig["fused_mul_recurrent_rwkv7"] = layer.fused_mul_recurrent_rwkv7
         _orig["chunk_rwkv7"] = layer.chunk_rwkv7
+        _orig["forward"] = layer.RWKV7Attention.forward
     layer.fused_mul_recurrent_rwkv7 = fused_mul_recurrent_rwkv7
     layer.chunk_rwkv7 = chunk_rwkv7
+    layer.RWKV7Attention.forward = (_fused_time_mix_forward if fuse_time_mix
+                                    else _orig["forward"])
 
 
 def uninstall() -> None:
-    """Restores fla's own ops."""
+    """Restores fla's own ops and forward."""
     import fla.layers.rwkv7 as layer
     for name, fn in _orig.items():
-        setattr(layer, name, fn)
+        if name == "forward":
+            layer.RWKV7Attention.forward = fn
+        else:
+            setattr(layer, name, fn)
     _orig.clear()
 
 

@@ -518,3 +518,33 @@ def slot_gather_outer_major(family: torch.Tensor, slot_dim: int, ids,
                   _ptr(out), n * row, row, _ptr(status_word(family.device)),
                   _stream(family.device))
     return out
+
+
+def wkv7_timemix_decode_slots(r, w_raw, k, v, v_first, v_raw, a_raw, g, k_k, k_a, r_k, gn_w,
+                              gn_b, gn_eps: float, bank_wkv: torch.Tensor, layer: int, slot_ids,
+                              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused RWKV-7 time-mix decode core (fla RWKV7Attention between its
+    projections and o_proj, one token): gates, v lerp, kk norm, k update, the
+    in-place WKV step of bank_wkv[layer, slot_ids], GroupNorm, correction and
+    output gate. Activations [B, 1, H*64] (or [B, H*64]); v_first / v_raw
+    None for layer 0. Returns o [B, 1, H*64] (input to o_proj)."""
+    _require_cuda(r, k, v, bank_wkv)
+    layer_t = _bank_layer(bank_wkv, layer)
+    Hn, K = layer_t.shape[1], layer_t.shape[2]
+    B = r.shape[0]
+    dt_t = r.dtype
+    acts = [r, w_raw, k, v, a_raw, g] + ([v_first, v_raw] if v_first is not None else [])
+    acts = [t.to(dt_t).contiguous() for t in acts]
+    r_, w_, k_, v_, a_, g_ = acts[:6]
+    vf_, vr_ = (acts[6], acts[7]) if v_first is not None else (None, None)
+    params = [t.to(dt_t).contiguous() for t in (k_k, k_a, r_k, gn_w, gn_b)]
+    ids = slot_ids_tensor(slot_ids, layer_t.shape[0], r.device)
+    if ids.numel() != B:
+        raise ValueError(f"{ids.numel()} slot ids for a batch of {B}")
+    o = torch.empty_like(r_) if out is None else out
+    with torch.cuda.device(r.device):
+        _lib.call("wkvm_wkv7_timemix_decode_slots", _ptr(r_), _ptr(w_), _ptr(k_), _ptr(v_),
+                  _ptr(vf_), _ptr(vr_), _ptr(a_), _ptr(g_), *(_ptr(t) for t in params), _ptr(o),
+                  _ptr(layer_t), layer_t.shape[0], _ptr(ids), B, Hn, K, float(gn_eps),
+                  _DTYPES[dt_t], _ptr(status_word(r.device)), _stream(r.device))
+    return o
