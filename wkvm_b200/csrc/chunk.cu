@@ -38,7 +38,8 @@ namespace {
 
 constexpr int CH = 64;             // chunk length
 constexpr int HD = 64;             // head dim (K == V)
-constexpr int NTHREADS = 256;      // two warps per TMEM lane quarter
+constexpr int NTHREADS = 512;      // four warps per TMEM lane quarter
+constexpr int CW = 64 / (NTHREADS / 128);  // columns of a row each thread takes
 constexpr int NIN = 6;             // r, w, k, v, x5, x6 input streams
 constexpr uint32_t LBO = 128;      // K-adjacent core matrices
 constexpr uint32_t SBO = 2048;     // 8-row groups of a 64-wide K tile
@@ -113,9 +114,9 @@ __device__ __forceinline__ void stg8(const uint8_t* sm, int in, int t, int k, fl
 }
 
 template <typename T>
-__device__ __forceinline__ void store_row32(T* dst, const float (&v)[32]) {
+__device__ __forceinline__ void store_row(T* dst, const float (&v)[CW]) {
 #pragma unroll
-  for (int i = 0; i < 32; i += 8) {
+  for (int i = 0; i < CW; i += 8) {
     uint4 u;
     T* e = reinterpret_cast<T*>(&u);
 #pragma unroll
@@ -139,8 +140,8 @@ __device__ __forceinline__ float in_b(const uint8_t* sm, int t, int k) {
   return MUL ? stg<T>(sm, IN_5, t, k) * x6 : x6;
 }
 
-// Thread roles: warp w serves TMEM lane quarter (w & 3); the two warps of a
-// quarter split the 64 columns of each row into halves g = w >> 2. A thread's
+// Thread roles: warp w serves TMEM lane quarter (w & 3); the four warps of a
+// quarter split the 64 columns of each row into groups g = w >> 2. A thread's
 // accumulator row is l = 32 (w & 3) + lane; rows 0..63 ("lo") carry the
 // a/k-side and state rows, rows 64..127 the r/b-side and output rows.
 template <typename Tin, bool MUL>
@@ -156,11 +157,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3;
-  const int g = warp >> 2;                 // column half
+  const int g = warp >> 2;                 // column group
   const int l = quarter * 32 + lane;       // accumulator row / TMEM lane
   const bool lo = l < 64;
   const int r64 = l & 63;
-  const int c0 = g * 32;                   // first column of this thread's half
+  const int c0 = g * CW;                   // first column of this thread's half
   const int H = p.H;
   const int n = blockIdx.x / H;
   const int hh = blockIdx.x - n * H;
@@ -221,22 +222,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
 
   // Issues 16-byte async copies of chunk c's six 64 x 64 input tiles into the
   // staging area (rows past the sequence end are zero-filled).
-  // Thread tid copies piece (tid & 7) of rows t = (tid >> 3) + 32 * (j & 1) of
-  // input stream j >> 1, for j = 0..11.
-  static_assert(NTHREADS == 256 && NIN * CH * 8 == 12 * NTHREADS, "staging map");
+  // Thread tid copies piece (tid & 7) of row t = (tid >> 3) & 63 of input
+  // streams (tid >> 9) + j, j stepping by NTHREADS / 512.
+  static_assert(NIN * CH * 8 % NTHREADS == 0, "staging map");
   auto stage = [&](int c) {
     const int64_t t0 = bos + (int64_t)c * CH;
     const int64_t rem = len - (int64_t)c * CH;
     const int cl = rem < CH ? (int)rem : CH;
     const uint32_t base = tc::smem_u32(sm + S_STG);
     const int piece = tid & 7;
-    const int trow = tid >> 3;
     const int64_t gstride = (int64_t)H * HD * 2;  // bytes between tokens
     const int64_t goff = (t0 * H + hh) * HD * 2 + piece * 16;
 #pragma unroll
-    for (int j = 0; j < 12; ++j) {
-      const int in = j >> 1;
-      const int t = trow + 32 * (j & 1);
+    for (int j = 0; j < NIN * CH * 8 / NTHREADS; ++j) {
+      const int e = tid + NTHREADS * j;
+      const int in = e >> 9;
+      const int t = (e >> 3) & 63;
       const uint32_t off = (in * CH + t) * STG_ROW + piece * 16;
       if (t < cl) cp_async16(base + off, gin[in] + goff + t * gstride);
       else *reinterpret_cast<uint4*>(sm + S_STG + off) = make_uint4(0, 0, 0, 0);
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
         acc += stg<Tin>(sm, IN_W, t, k);
         Grow[t * RS + k] = acc;
       }
-    } else {
+    } else if (tid < 256) {
       const int v = tid & 63, t0 = ((tid - 128) >> 6) * 32;
 #pragma unroll
       for (int t = t0; t < t0 + 32; t += 4) {
@@ -298,9 +299,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     //          hi rows t: r~ -> TMEM, b~ -> B tile row 64+t, r e^G -> TMEM.
     {
       const int t = r64;
-      float av[32], xg[32];
+      float av[CW], xg[CW];
 #pragma unroll
-      for (int k8 = 0; k8 < 32; k8 += 8) {
+      for (int k8 = 0; k8 < CW; k8 += 8) {
         const int k0 = c0 + k8;
         float x[8], wv[8], y[8], z[8], gt[8];
         stg8<Tin>(sm, IN_W, t, k0, wv);
@@ -339,8 +340,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
         kst4(sm + S_RB, l, k0, make_float4(bt[0], bt[1], bt[2], bt[3]));
         kst4(sm + S_RB, l, k0 + 4, make_float4(bt[4], bt[5], bt[6], bt[7]));
       }
-      tc::tmem_st32(tq + T_A1 + c0, av);
-      if (!lo) tc::tmem_st32(tq + T_RG + c0, xg);
+      tc::tmem_st(tq + T_A1 + c0, av);
+      if (!lo) tc::tmem_st(tq + T_RG + c0, xg);
       tc::tmem_st_wait();
     }
     sync_tc();
@@ -363,24 +364,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
       const int t = r64;
 #pragma unroll 1
       for (int h2 = 0; h2 < 2; ++h2) {  // h2 = 0: x k~ columns, 1: x b~ columns
-        float x[32];
+        float x[CW];
         const uint32_t ta = tq + T_D1 + h2 * 64 + c0;
-        tc::tmem_ld32(ta, x);
+        tc::tmem_ld(ta, x);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < CW; ++i) {
           const int s = c0 + i;
           const bool keep = lo ? (s < t) : (s <= t);
           x[i] = keep ? x[i] : 0.f;
         }
         if (lo && h2 == 1) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) st4(&Aab[t * RS + c0 + i], &x[i]);
+          for (int i = 0; i < CW; i += 4) st4(&Aab[t * RS + c0 + i], &x[i]);
         } else if (lo) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
+          for (int i = 0; i < CW; i += 4)
             kst4(sm + S_AK, t, c0 + i, make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
         } else {
-          tc::tmem_st32(ta, x);
+          tc::tmem_st(ta, x);
         }
       }
       tc::tmem_st_wait();
@@ -403,26 +404,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     //      hi: (a e^Gx)^T -> T_A1 lanes 64+k, under (A_ak V)^T in lanes 0..63.
     {
       const int k = r64;
-      float x[32], y[32];
+      float x[CW], y[CW];
       if (lo) {
         const float gc = Grow[63 * RS + k];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < CW; ++i) {
           const int t = c0 + i;
           const float e = __expf(gc - Grow[t * RS + k]);
           x[i] = stg<Tin>(sm, IN_K, t, k) * e;
           y[i] = in_b<Tin, MUL>(sm, t, k) * e;
         }
-        tc::tmem_st32(tq + T_D1 + c0, x);
-        tc::tmem_st32(tq + T_D1 + 64 + c0, y);
+        tc::tmem_st(tq + T_D1 + c0, x);
+        tc::tmem_st(tq + T_D1 + 64 + c0, y);
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < CW; ++i) {
           const int t = c0 + i;
           const float a = stg<Tin>(sm, IN_5, t, k);
           x[i] = (MUL ? -a : a) * __expf(Grow[t * RS + k] - stg<Tin>(sm, IN_W, t, k));
         }
-        tc::tmem_st32(tq + T_A1 + c0, x);
+        tc::tmem_st(tq + T_A1 + c0, x);
       }
       tc::tmem_st_wait();
     }
@@ -434,7 +435,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     if (c + 1 < nchunks) stage(c + 1);
 
     // ---- T = (I - A_ab)^-1 as a K-major tile (row t', K = t); G is spent
-    chunkc::tri_inverse64(Aab, Grow, sm + S_TT, tid);
+    chunkc::tri_inverse64(Aab, Grow, sm + S_TT, tid);  // threads >= 256 only synchronise
     sync_tc();
 
     // ---- MMA S: [(A_ak V)^T; (a e^Gx)^T] x T^T -> T_D3 = [U~^T; W^T]
@@ -447,11 +448,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     }
     if (!wait_mma()) { failed = true; break; }
     {  // [W^T; U~^T] B tile: lane l < 64 holds U~^T row l, lane 64+j holds W^T row j
-      float x[32];
-      tc::tmem_ld32(tq + T_D3 + c0, x);
+      float x[CW];
+      tc::tmem_ld(tq + T_D3 + c0, x);
       const int row = lo ? 64 + l : l - 64;
 #pragma unroll
-      for (int i = 0; i < 32; i += 4)
+      for (int i = 0; i < CW; i += 4)
         kst4(sm + S_RB, row, c0 + i, make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
     }
     sync_tc();
@@ -477,21 +478,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
 
     // ---- M = diag(e^G_C) + Bh^T W (lanes k), P = r e^G + A_qb W (lanes 64+t)
     {
-      float x[32];
+      float x[CW];
       const uint32_t ta = tq + T_A1 + c0;
-      tc::tmem_ld32(ta, x);
+      tc::tmem_ld(ta, x);
       if (lo) {
         const int k = r64;
         const float d = s_gc[k];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[i] += (c0 + i == k) ? d : 0.f;
+        for (int i = 0; i < CW; ++i) x[i] += (c0 + i == k) ? d : 0.f;
       } else {
-        float rg[32];
-        tc::tmem_ld32(tq + T_RG + c0, rg);
+        float rg[CW];
+        tc::tmem_ld(tq + T_RG + c0, rg);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[i] += rg[i];
+        for (int i = 0; i < CW; ++i) x[i] += rg[i];
       }
-      tc::tmem_st32(ta, x);
+      tc::tmem_st(ta, x);
       tc::tmem_st_wait();
     }
     sync_tc();
@@ -507,22 +508,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     if (!wait_mma()) { failed = true; break; }
 
     {
-      float x[32];
-      tc::tmem_ld32(tq + T_D3 + c0, x);
+      float x[CW];
+      tc::tmem_ld(tq + T_D3 + c0, x);
       if (lo) {
         const int k = r64;  // S'[k][v]: column k of S^T
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
+        for (int i = 0; i < CW; ++i)
           *reinterpret_cast<float*>(sm + S_ST + tc::kmajor_off(c0 + i, k, LBO_S, SBO_S)) = x[i];
         if (last && p.h_out) {
           float* dst = p.h_out + hoff + k * HD + c0;
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
+          for (int i = 0; i < CW; i += 4)
             st_stream_f4(dst + i, make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
         }
       } else {
         const int t = r64;
-        if (t < clen) store_row32(go + ((tok0 + t) * H + hh) * HD + c0, x);
+        if (t < clen) store_row(go + ((tok0 + t) * H + hh) * HD + c0, x);
       }
     }
     sync_tc();

@@ -30,86 +30,101 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // substitution, then T_ij = T_ii A_ij T_jj for the off-diagonal blocks.
 // Written as a K-major tf32 operand tile (row t', K = t; LBO 128, SBO 2048),
 // zero above the diagonal. Trow is row-major scratch (stride RS). Must be
-// called by all 256 threads of the CTA; ends with a __syncthreads-free tile
-// write (the caller fences and synchronises before the tensor core reads it).
+// called by every thread of the CTA (256 or more); threads 256 and up only
+// take part in the barriers. Ends with the tile write, without a barrier
+// (the caller fences and synchronises before the tensor core reads it).
 __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, float* Trow,
                                               uint8_t* tt_tile, int tid) {
-    {
-    float* Tr = Trow;
-    if (tid < 64) {  // diagonal 16 x 16 blocks, one column per thread
-      const int col = tid, b0 = col & ~15, ci = col & 15;
-      float y[16];
+  float* Tr = Trow;
+  const bool act = tid < 256;
+  if (tid < 64) {  // diagonal 16 x 16 blocks, one column per thread
+    const int col = tid, b0 = col & ~15, ci = col & 15;
+    float y[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float v = (i == ci) ? 1.f : 0.f;
+    for (int i = 0; i < 16; ++i) {
+      float v = (i == ci) ? 1.f : 0.f;
 #pragma unroll
-        for (int i2 = 0; i2 < i; ++i2) v = fmaf(Aab[(b0 + i) * RS + b0 + i2], y[i2], v);
-        y[i] = (i < ci) ? 0.f : v;
-        Tr[(b0 + i) * RS + col] = y[i];
+      for (int i2 = 0; i2 < i; ++i2) v = fmaf(Aab[(b0 + i) * RS + b0 + i2], y[i2], v);
+      y[i] = (i < ci) ? 0.f : v;
+      Tr[(b0 + i) * RS + col] = y[i];
+    }
+  }
+  __syncthreads();
+  // blocks (1,0) and (3,2) of 16: X = A T_jj, then T_ij = T_ii X.
+  // Thread: row r = (tid >> 4) & 15, column cc = tid & 15 of both blocks.
+  const int r = (tid >> 4) & 15, cc = tid & 15;
+  float xv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (act) {
+#pragma unroll
+    for (int s2 = 0; s2 < 16; ++s2) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float tv = Tr[(32 * q + s2) * RS + 32 * q + cc];
+        const float av = Aab[(32 * q + 16 + r) * RS + 32 * q + s2];
+        xv[q] = fmaf(av, s2 >= cc ? tv : 0.f, xv[q]);
       }
     }
-    __syncthreads();
-    {  // blocks (1,0) and (3,2) of 16: X = A T_jj, then T_ij = T_ii X.
-       // Thread: row r = (tid >> 4) & 15, column cc = tid & 15 of both blocks.
-      const int r = (tid >> 4) & 15, cc = tid & 15;
-      float xv[2] = {0.f, 0.f};
 #pragma unroll
-      for (int s2 = 0; s2 < 16; ++s2) {
+    for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[q];
+  }
+  __syncthreads();
+  if (act) {
+    float yv[2] = {0.f, 0.f};
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const float tv = Tr[(32 * q + s2) * RS + 32 * q + cc];
-          const float av = Aab[(32 * q + 16 + r) * RS + 32 * q + s2];
-          xv[q] = fmaf(av, s2 >= cc ? tv : 0.f, xv[q]);
-        }
+    for (int s2 = 0; s2 < 16; ++s2) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float tv = Tr[(32 * q + 16 + r) * RS + 32 * q + 16 + s2];
+        const float xx = Tr[(32 * q + 16 + s2) * RS + 32 * q + cc];
+        yv[q] = fmaf(s2 <= r ? tv : 0.f, xx, yv[q]);
       }
-      if (tid < 256) {
-#pragma unroll
-        for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[q];
-      }
-      __syncthreads();
-      float yv[2] = {0.f, 0.f};
-#pragma unroll
-      for (int s2 = 0; s2 < 16; ++s2) {
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const float tv = Tr[(32 * q + 16 + r) * RS + 32 * q + 16 + s2];
-          const float xx = Tr[(32 * q + 16 + s2) * RS + 32 * q + cc];
-          yv[q] = fmaf(s2 <= r ? tv : 0.f, xx, yv[q]);
-        }
-      }
-      __syncthreads();
-#pragma unroll
-      for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = yv[q];
     }
-    __syncthreads();
-    {  // block (1,0) of 32: X = A T_00, then T_10 = T_11 X. Thread: column
-       // C = tid & 31, rows 32 + (tid >> 5) + 8 q.
-      const int C = tid & 31, r0 = tid >> 5;
-      float xv[4] = {0.f, 0.f, 0.f, 0.f};
+    xv[0] = yv[0];
+    xv[1] = yv[1];
+  }
+  __syncthreads();
+  if (act) {
 #pragma unroll
-      for (int s2 = 0; s2 < 32; ++s2) {
-        const float tv = s2 >= C ? Tr[s2 * RS + C] : 0.f;
+    for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[q];
+  }
+  __syncthreads();
+  // block (1,0) of 32: X = A T_00, then T_10 = T_11 X. Thread: column
+  // C = tid & 31, rows 32 + (tid >> 5) + 8 q.
+  const int C = tid & 31, r0 = (tid >> 5) & 7;
+  if (act) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) xv[q] = fmaf(Aab[(32 + r0 + 8 * q) * RS + s2], tv, xv[q]);
-      }
+    for (int q = 0; q < 4; ++q) xv[q] = 0.f;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = xv[q];
-      __syncthreads();
-      float yv[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s2 = 0; s2 < 32; ++s2) {
+      const float tv = s2 >= C ? Tr[s2 * RS + C] : 0.f;
 #pragma unroll
-      for (int s2 = 0; s2 < 32; ++s2) {
-        const float xx = Tr[(32 + s2) * RS + C];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int R = r0 + 8 * q;
-          yv[q] = fmaf(s2 <= R ? Tr[(32 + R) * RS + 32 + s2] : 0.f, xx, yv[q]);
-        }
-      }
-      __syncthreads();
-#pragma unroll
-      for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = yv[q];
+      for (int q = 0; q < 4; ++q) xv[q] = fmaf(Aab[(32 + r0 + 8 * q) * RS + s2], tv, xv[q]);
     }
-    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = xv[q];
+  }
+  __syncthreads();
+  if (act) {
+    float yv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s2 = 0; s2 < 32; ++s2) {
+      const float xx = Tr[(32 + s2) * RS + C];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int R = r0 + 8 * q;
+        yv[q] = fmaf(s2 <= R ? Tr[(32 + R) * RS + 32 + s2] : 0.f, xx, yv[q]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) xv[q] = yv[q];
+  }
+  __syncthreads();
+  if (act) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = xv[q];
+  }
+  __syncthreads();
+  if (act) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {  // K-major tile, zero above the diagonal;
       // lanes walk 8 rows x 4 K-quads so each store instruction fills 512
