@@ -211,16 +211,28 @@ int wkvm_dplr_prefill_slots(
 /* Chunked GDN prefill: replaces fla `chunk_gated_delta_rule`
  * (fla/ops/gated_delta_rule/chunk.py:365, forward :29-116) for head-wise g
  * and beta, [K,V] state layout. Arguments as for
- * wkvm_fused_recurrent_gated_delta_rule. K == V == 128 with 16-bit inputs
- * runs the tcgen05 tf32 chunk kernel (one CTA per sequence, value head and
- * half of V); other shapes run the recurrent kernel. */
+ * wkvm_fused_recurrent_gated_delta_rule, plus a device workspace the caller
+ * owns. K == V == 128 with 16-bit inputs runs on the tcgen05 tensor core:
+ * with a workspace of at least one window (see
+ * wkvm_gdn_chunk_workspace_bytes) as two launches, a chunk-parallel WY
+ * kernel and a sequential state pass; without one as a single kernel (one
+ * CTA per sequence, value head and half of V). Other shapes run the
+ * recurrent kernel. The workspace is 256-byte aligned or ignored. */
 int wkvm_chunk_gated_delta_rule(
     const void* q, const void* k, const void* v, const void* g,
     const void* beta, void* o,
     const float* h0, float* ht, const int64_t* cu_seqlens,
     int32_t B, int32_t T, int32_t H, int32_t HV, int32_t K, int32_t V,
     float scale, int32_t use_qk_l2norm, int32_t dtype,
+    void* workspace, int64_t workspace_bytes,
     int32_t* status, wkvm_stream_t stream);
+
+/* Workspace bytes for the two-launch GDN prefill of nseq sequences of at
+ * most T tokens (T = total tokens with cu_seqlens) in one window; 0 when the
+ * shape does not take that path. A smaller workspace (at least
+ * nseq*HV*(64 KiB + one chunk record) bytes) processes the chunks in
+ * windows. */
+int64_t wkvm_gdn_chunk_workspace_bytes(int32_t nseq, int32_t T, int32_t HV, int32_t K, int32_t V);
 
 /* Slot-native chunked GDN prefill: initial and final state of sequence i
  * in bank_layer[slot_ids[i]] ([num_slots, HV, K, V] fp32). No wkvm caller
@@ -232,6 +244,7 @@ int wkvm_gdn_prefill_slots(
     const int64_t* cu_seqlens,
     int32_t B, int32_t T, int32_t H, int32_t HV, int32_t K, int32_t V,
     float scale, int32_t use_qk_l2norm, int32_t dtype,
+    void* workspace, int64_t workspace_bytes,
     int32_t* status, wkvm_stream_t stream);
 
 /* ------------------------------------------------------------------------

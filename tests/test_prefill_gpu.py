@@ -124,10 +124,19 @@ def test_other_head_dims_use_recurrent_path(cuda):
 GDN = ("q", "k", "v", "g", "beta")
 
 
+@pytest.fixture(params=["two_phase", "windowed", "one_kernel"])
+def gdn_path(request, monkeypatch):
+    """GDN prefill path: two launches over a full workspace, the same with a
+    one-chunk window (state carried between windows), or the fused kernel."""
+    limit = {"two_phase": prefill.GDN_WORKSPACE_LIMIT, "windowed": 1, "one_kernel": 0}
+    monkeypatch.setattr(prefill, "GDN_WORKSPACE_LIMIT", limit[request.param])
+    return request.param
+
+
 @pytest.mark.parametrize("T", [1, 100, 200])
 @pytest.mark.parametrize("hv_mult", [1, 2])
 @pytest.mark.parametrize("l2", [False, True])
-def test_chunk_gdn_matches_oracle(cuda, T, hv_mult, l2):
+def test_chunk_gdn_matches_oracle(cuda, gdn_path, T, hv_mult, l2):
     B, H, K = 2, 2, 128
     x = synth.gdn_inputs(B, T, H, K, HV=H * hv_mult, seed=T + hv_mult)
     if l2:
@@ -144,7 +153,7 @@ def test_chunk_gdn_matches_oracle(cuda, T, hv_mult, l2):
     assert rel_err(ht, rh) < REL_TOL
 
 
-def test_chunk_gdn_4096_tokens(cuda):
+def test_chunk_gdn_4096_tokens(cuda, gdn_path):
     B, T, H, K = 1, 4096, 2, 128
     x = synth.gdn_inputs(B, T, H, K, seed=31)
     d = _to(x, cuda)
@@ -155,7 +164,7 @@ def test_chunk_gdn_4096_tokens(cuda):
     assert rel_err(ht, rh) < REL_TOL
 
 
-def test_gdn_prefill_slots_varlen(cuda):
+def test_gdn_prefill_slots_varlen(cuda, gdn_path):
     S, HV, K = 6, 2, 128
     lens = [70, 0, 130]
     ids = [4, 2, 5]

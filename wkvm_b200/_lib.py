@@ -42,8 +42,14 @@ SIGNATURES: dict[str, list] = {
     "wkvm_chunk_dplr": [P] * 7 + [P, P, P] + [I32] * 5 + [F32, I32, P, P],
     "wkvm_wkv7_prefill_slots": [P] * 7 + [P, I64, P, P] + [I32] * 5 + [I32, P, P],
     "wkvm_dplr_prefill_slots": [P] * 7 + [P, I64, P, P] + [I32] * 5 + [F32, I32, P, P],
-    "wkvm_chunk_gated_delta_rule": [P] * 6 + [P, P, P] + [I32] * 6 + [F32, I32, I32, P, P],
-    "wkvm_gdn_prefill_slots": [P] * 6 + [P, I64, P, P] + [I32] * 6 + [F32, I32, I32, P, P],
+    "wkvm_chunk_gated_delta_rule": [P] * 6 + [P, P, P] + [I32] * 6 + [F32, I32, I32, P, I64, P, P],
+    "wkvm_gdn_prefill_slots": [P] * 6 + [P, I64, P, P] + [I32] * 6 + [F32, I32, I32, P, I64, P, P],
+    "wkvm_gdn_chunk_workspace_bytes": [I32] * 5,
+}
+
+RESTYPES = {
+    "wkvm_strerror": ctypes.c_char_p,
+    "wkvm_gdn_chunk_workspace_bytes": ctypes.c_int64,
 }
 
 ERR_NAMES = {
@@ -86,7 +92,7 @@ def load(path: Path | str | None = None):
             if fn is None:
                 continue
             fn.argtypes = argtypes
-            fn.restype = ctypes.c_char_p if name == "wkvm_strerror" else ctypes.c_int
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
         _lib = lib
         return lib
 

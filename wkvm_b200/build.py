@@ -16,7 +16,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libwkvm_b200.so"
-SOURCES = ["recurrent.cu", "slots.cu", "selftest.cu", "chunk.cu", "gdn_chunk.cu", "timemix.cu"]
+SOURCES = ["recurrent.cu", "slots.cu", "selftest.cu", "chunk.cu", "gdn_chunk.cu", "gdn_wy.cu",
+           "timemix.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUTLASS_INCLUDE_CANDIDATES = [
     Path(sys.prefix) / "lib/python3.12/site-packages/flashinfer/data/cutlass/include",

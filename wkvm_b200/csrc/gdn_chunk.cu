@@ -545,6 +545,13 @@ int run_gdn_chunk(const GdnArgs& a, int nseq, int dtype, cudaStream_t stream) {
 }
 
 }  // namespace
+
+int gdn_two_phase(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                  void* o, const float* h_in, float* h_out, bool slots, const int32_t* ids,
+                  int64_t num_slots, const int64_t* cu, int nseq, int T, int H, int HV,
+                  float scale, bool l2norm, int dtype, void* workspace, int64_t ws_bytes,
+                  int* status, cudaStream_t stream);
+
 }  // namespace wkvm
 
 extern "C" int wkvm_fused_recurrent_gated_delta_rule(
@@ -561,7 +568,8 @@ extern "C" int wkvm_chunk_gated_delta_rule(const void* q, const void* k, const v
                                            const float* h0, float* ht, const int64_t* cu_seqlens,
                                            int32_t B, int32_t T, int32_t H, int32_t HV, int32_t K,
                                            int32_t V, float scale, int32_t use_qk_l2norm,
-                                           int32_t dtype, int32_t* status,
+                                           int32_t dtype, void* workspace,
+                                           int64_t workspace_bytes, int32_t* status,
                                            wkvm_stream_t stream) {
   if (!wkvm::gdn_chunk_ok(K, V, dtype, q, k, v, o))
     return wkvm_fused_recurrent_gated_delta_rule(q, k, v, g, beta, o, h0, ht, cu_seqlens, B, T, H,
@@ -571,6 +579,12 @@ extern "C" int wkvm_chunk_gated_delta_rule(const void* q, const void* k, const v
   if (B == 0) return WKVM_OK;
   if (!g || !beta) return WKVM_ERR_INVALID_ARG;
   if ((h0 && !wkvm::al16(h0)) || (ht && !wkvm::al16(ht))) return WKVM_ERR_ALIGN;
+  if (workspace) {
+    const int r = wkvm::gdn_two_phase(q, k, v, g, beta, o, h0, ht, false, nullptr, 0, cu_seqlens,
+                                      B, T, H, HV, scale, use_qk_l2norm != 0, dtype, workspace,
+                                      workspace_bytes, status, (cudaStream_t)stream);
+    if (r != WKVM_ERR_UNSUPPORTED) return r;
+  }
   wkvm::GdnArgs a{q, k, v, g, beta, o, h0, ht, nullptr, 0, cu_seqlens, T, H, HV, scale,
                   use_qk_l2norm != 0, status};
   return wkvm::run_gdn_chunk(a, B, dtype, (cudaStream_t)stream);
@@ -581,7 +595,8 @@ extern "C" int wkvm_gdn_prefill_slots(const void* q, const void* k, const void* 
                                       int64_t num_slots, const int32_t* slot_ids,
                                       const int64_t* cu_seqlens, int32_t B, int32_t T, int32_t H,
                                       int32_t HV, int32_t K, int32_t V, float scale,
-                                      int32_t use_qk_l2norm, int32_t dtype, int32_t* status,
+                                      int32_t use_qk_l2norm, int32_t dtype, void* workspace,
+                                      int64_t workspace_bytes, int32_t* status,
                                       wkvm_stream_t stream) {
   if (!bank_layer || num_slots <= 0 || (B > 0 && !slot_ids)) return WKVM_ERR_INVALID_ARG;
   if (!wkvm::gdn_chunk_ok(K, V, dtype, q, k, v, o)) {
@@ -593,6 +608,13 @@ extern "C" int wkvm_gdn_prefill_slots(const void* q, const void* k, const void* 
   if (B == 0) return WKVM_OK;
   if (!g || !beta) return WKVM_ERR_INVALID_ARG;
   if (!wkvm::al16(bank_layer)) return WKVM_ERR_ALIGN;
+  if (workspace) {
+    const int r = wkvm::gdn_two_phase(q, k, v, g, beta, o, bank_layer, bank_layer, true, slot_ids,
+                                      num_slots, cu_seqlens, B, T, H, HV, scale,
+                                      use_qk_l2norm != 0, dtype, workspace, workspace_bytes,
+                                      status, (cudaStream_t)stream);
+    if (r != WKVM_ERR_UNSUPPORTED) return r;
+  }
   wkvm::GdnArgs a{q, k, v, g, beta, o, bank_layer, bank_layer, slot_ids, num_slots, cu_seqlens,
                   T, H, HV, scale, use_qk_l2norm != 0, status};
   return wkvm::run_gdn_chunk(a, B, dtype, (cudaStream_t)stream);

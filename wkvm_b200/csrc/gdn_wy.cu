@@ -1,0 +1,683 @@
+// Two-phase chunked prefill of the gated delta rule (K = V = 128) on the
+// sm_100a tensor core (tcgen05.mma kind::tf32, fp32 accumulators in TMEM).
+//
+// Only a small part of a chunk's work depends on the incoming state, so it is
+// split in two launches:
+//
+//  phase 1, gdn_wy_kernel: one CTA per (chunk, sequence, value head), all
+//    chunks at once. Builds the chunk's WY factors and writes one record:
+//      A[t][s] = beta_t e^(G_t-G_s) k^_t.k^_s (s < t),  T = (I + A)^-1
+//      U = T (beta v),  W = T (beta e^G k^)                     (u = U - W S)
+//      Q~ = scale e^G q^,  K~ = e^(G_C-G) k^,
+//      A_qk[t][s] = scale e^(G_t-G_s) q^_t.k^_s (s <= t)
+//  phase 2, gdn_state_kernel: one CTA per (sequence, value head) walks the
+//    chunks in order with the state S^T (rows v, columns k) resident in TMEM:
+//      [(W S)^T | (Q~ S)^T] = S^T [W; Q~]^T                    (MMA A)
+//      u^T = U^T - (W S)^T,  S^T <- e^(G_C) S^T
+//      S^T += u^T K~,  (Q~ S)^T += u^T A_qk^T = O^T            (MMA B)
+//
+// The derivation (decay first, then the delta update, per token) follows
+// fla's recurrence fla/ops/gated_delta_rule/fused_recurrent.py:128-151 and
+// the chunk form of fla/ops/gated_delta_rule/chunk.py:29-116; operand
+// orientation, record layout and the TMEM-resident state are this file's own.
+//
+// Records live in a caller-provided workspace; when it is smaller than the
+// whole prefill needs, the sequences are processed in windows of chunks and
+// the state is carried between windows in the workspace.
+#include "chunk_common.cuh"
+
+namespace wkvm {
+
+namespace gdnwy {
+
+constexpr int CH = 64, KD = 128, VD = 128;
+constexpr uint32_t LBO = 128;
+constexpr uint32_t SBO64 = 2048, SBO128 = 4096;  // K = 64 / K = 128 tiles
+constexpr uint32_t KSTEP = 2 * LBO;              // 8 tf32 of K per MMA
+
+// record layout (bytes)
+constexpr uint32_t R_WQ = 0;                 // [W; Q~]: 128 rows x K = 128 (k), SBO 4096
+constexpr uint32_t R_KT = R_WQ + 65536;      // K~^T: 128 rows (k) x K = 64 (t), SBO 2048
+constexpr uint32_t R_AQK = R_KT + 32768;     // A_qk: 64 rows (t) x K = 64 (s), SBO 2048
+constexpr uint32_t R_U = R_AQK + 16384;      // U: 64 rows (t) x 128 v, row-major
+constexpr uint32_t R_META = R_U + 32768;     // e^(G_C)
+constexpr uint32_t REC_BYTES = R_META + 128;
+constexpr uint32_t PART_A = R_KT - R_WQ;             // loaded first (MMA A)
+constexpr uint32_t PART_B = R_META + 16 - R_KT;      // the rest
+static_assert(REC_BYTES % 128 == 0 && PART_B % 16 == 0, "record alignment");
+
+}  // namespace gdnwy
+
+namespace {
+
+using namespace gdnwy;
+using chunkc::RS;
+
+struct WyArgs {
+  const void *q, *k, *v, *g, *beta;
+  uint8_t* ws;        // records [nseq][W][HV]
+  const int64_t* cu;
+  int T, H, HV, w0, W;
+  float scale;
+  bool l2norm;
+  int* status;
+};
+
+struct StateArgs {
+  const uint8_t* ws;
+  void* o;
+  const float* h_src;   // state entering the window (nullptr: zeros)
+  float* h_dst;         // state leaving the window (nullptr: dropped)
+  bool src_slots, dst_slots;  // index h_src / h_dst by slot id (else by sequence)
+  const int32_t* ids;
+  int64_t num_slots;
+  const int64_t* cu;
+  int T, HV, w0, W;
+  int* status;
+};
+
+__device__ __forceinline__ void sync_tc() {
+  tc::fence_smem_to_async();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+}
+
+__device__ __forceinline__ float sel4(float a0, float a1, float a2, float a3, int i) {
+  return i == 0 ? a0 : i == 1 ? a1 : i == 2 ? a2 : a3;
+}
+
+// 4 x 4 transpose inside each quad of lanes: on entry lane q of the quad holds
+// a[c] = M[c][q]; on exit it holds b[r] = M[q][r].
+__device__ __forceinline__ float4 quad_transpose(const float (&a)[4], int lane) {
+  const int q = lane & 3;
+  float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+#pragma unroll
+  for (int d = 0; d < 4; ++d) {
+    const int r = (q - d) & 3;  // source lane within the quad
+    const float send = sel4(a[0], a[1], a[2], a[3], (q + d) & 3);
+    const float got = d == 0 ? send : __shfl_sync(0xffffffffu, send, (lane & ~3) | r);
+    if (r == 0) b0 = got;
+    if (r == 1) b1 = got;
+    if (r == 2) b2 = got;
+    if (r == 3) b3 = got;
+  }
+  return make_float4(b0, b1, b2, b3);
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) &
+                                    ~static_cast<uintptr_t>(1023));
+}
+
+// ---------------------------------------------------------------- phase 1
+
+constexpr int WY_THREADS = 256;
+// shared memory: [k; q] tile (128 rows x K = 128, unnormalised) = 64 KiB.
+// After MMA 1 the same bytes hold -A (row-major), the inverse's scratch and
+// the T tile.
+constexpr uint32_t WS_XT = 0;
+constexpr uint32_t WS_AAB = 0;
+constexpr uint32_t WS_TR = WS_AAB + CH * RS * 4;
+constexpr uint32_t WS_TT = 36864;
+static_assert(WS_TR + CH * RS * 4 <= WS_TT, "inverse scratch overlaps the T tile");
+constexpr uint32_t KV_ROW = KD * 2 + 16;           // staged 16-bit k / v row (+16 pad)
+constexpr uint32_t WS_KST = 65536;                  // k rows, 16-bit
+constexpr uint32_t WS_VST = WS_KST + CH * KV_ROW;   // v rows, 16-bit
+constexpr uint32_t WY_SMEM = WS_VST + CH * KV_ROW + 1024;
+// TMEM: MMA 1 accumulator, later U^T | (beta v)^T | (beta e^G k^)^T | W^T
+constexpr uint32_t WY_TMEM_COLS = 256;
+constexpr uint32_t T_D1 = 0, T_AV = 64, T_AK = 128, T_DW = 192;
+
+template <typename Tin>
+__global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ float s_beta[CH], s_G[CH], s_eG[CH], s_eGC[CH], s_rk[CH], s_rq[CH];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, gh = warp >> 2;
+  const int l = quarter * 32 + lane;  // TMEM lane
+  const bool lo = l < 64;
+  const int r64 = l & 63;
+  const int n = blockIdx.y, hv = blockIdx.z;
+  const int H = p.H, HV = p.HV, hq = hv / (HV / H);
+  const int c = p.w0 + blockIdx.x;
+  int64_t bos, len;
+  if (p.cu) {
+    bos = p.cu[n];
+    len = p.cu[n + 1] - bos;
+  } else {
+    bos = (int64_t)n * p.T;
+    len = p.T;
+  }
+  if ((int64_t)c * CH >= len) return;  // past this sequence's end (uniform)
+  const int64_t tok0 = bos + (int64_t)c * CH;
+  const int clen = (len - (int64_t)c * CH) < CH ? (int)(len - (int64_t)c * CH) : CH;
+  uint8_t* rec = p.ws + (((int64_t)n * p.W + blockIdx.x) * HV + hv) * (int64_t)REC_BYTES;
+  const Tin* __restrict__ gq = static_cast<const Tin*>(p.q);
+  const Tin* __restrict__ gk = static_cast<const Tin*>(p.k);
+  const Tin* __restrict__ gv = static_cast<const Tin*>(p.v);
+
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_slot, WY_TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) tc::mbar_init(&mbar, 1);
+  {  // k and v rows -> shared memory (read column-wise for the TMEM operands)
+    const uint32_t base = tc::smem_u32(sm);
+#pragma unroll
+    for (int j = 0; j < 2 * CH * 16 / WY_THREADS; ++j) {
+      const int e = tid + WY_THREADS * j;
+      const int isv = e >> 10, t = (e >> 4) & 63, piece = e & 15;
+      const uint32_t off = (isv ? WS_VST : WS_KST) + t * KV_ROW + piece * 16;
+      const Tin* src = isv ? gv + ((tok0 + t) * HV + hv) * VD : gk + ((tok0 + t) * H + hq) * KD;
+      if (t < clen) chunkc::cp_async16(base + off, reinterpret_cast<const uint8_t*>(src) + piece * 16);
+      else *reinterpret_cast<uint4*>(sm + off) = make_uint4(0, 0, 0, 0);
+    }
+    chunkc::cp_async_commit();
+  }
+  // per-token decay and beta (warp 0; loads issued before the tile loads)
+  float ga = 0.f, gb2 = 0.f, ba = 0.f, bb = 0.f;
+  if (warp == 0) {
+    const Tin* gg = static_cast<const Tin*>(p.g);
+    const Tin* gb = static_cast<const Tin*>(p.beta);
+    if (lane < clen) {
+      ga = to_f32(gg[(tok0 + lane) * HV + hv]);
+      ba = to_f32(gb[(tok0 + lane) * HV + hv]);
+    }
+    if (lane + 32 < clen) {
+      gb2 = to_f32(gg[(tok0 + lane + 32) * HV + hv]);
+      bb = to_f32(gb[(tok0 + lane + 32) * HV + hv]);
+    }
+  }
+  // [k; q] rows -> fp32 K-major tile; squared norms per row
+  {
+    const int r = tid >> 1, half = tid & 1;
+    const int t = r & 63;
+    const bool isq = r >= 64;
+    const bool valid = t < clen;
+    const Tin* src = (isq ? gq : gk) + ((tok0 + t) * H + hq) * KD + half * 64;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (valid) u = __ldg(reinterpret_cast<const uint4*>(src) + j);
+      const Tin* e = reinterpret_cast<const Tin*>(&u);
+      float x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        x[i] = to_f32(e[i]);
+        ss = fmaf(x[i], x[i], ss);
+      }
+      const int k0 = half * 64 + j * 8;
+      chunkc::kst4(sm + WS_XT, r, k0, LBO, SBO128, make_float4(x[0], x[1], x[2], x[3]));
+      chunkc::kst4(sm + WS_XT, r, k0 + 4, LBO, SBO128, make_float4(x[4], x[5], x[6], x[7]));
+    }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    if (half == 0) {
+      const float f = p.l2norm ? 1.0f / sqrtf(ss + 1e-6f) : 1.f;
+      if (isq) s_rq[t] = f * p.scale;
+      else s_rk[t] = f;
+    }
+  }
+  if (warp == 0) {  // inclusive decay scan
+    float a = ga, b = gb2;
+    s_beta[lane] = ba;
+    s_beta[lane + 32] = bb;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float ua = __shfl_up_sync(0xffffffffu, a, off);
+      const float ub = __shfl_up_sync(0xffffffffu, b, off);
+      if (lane >= off) {
+        a += ua;
+        b += ub;
+      }
+    }
+    b += __shfl_sync(0xffffffffu, a, 31);
+    const float gc = __shfl_sync(0xffffffffu, b, 31);
+    s_G[lane] = a;
+    s_G[lane + 32] = b;
+    s_eG[lane] = __expf(a);
+    s_eG[lane + 32] = __expf(b);
+    s_eGC[lane] = __expf(gc - a);
+    s_eGC[lane + 32] = __expf(gc - b);
+  }
+  sync_tc();
+  const uint32_t tm = tmem_slot;
+  const uint32_t tq = tc::tmem_addr(tm, quarter * 32, 0);
+  const float GC = s_G[CH - 1];
+
+  // ---- MMA 1: [k; q] x k^T -> D1 (Gram blocks, unnormalised)
+  if (tid == 0) {
+    const uint32_t x0 = tc::smem_u32(sm + WS_XT);
+    for (int kk = 0; kk < KD / 8; ++kk)
+      tc::mma_tf32(tm + T_D1, tc::smem_desc(x0 + kk * KSTEP, LBO, SBO128),
+                   tc::smem_desc(x0 + kk * KSTEP, LBO, SBO128), tc::idesc_tf32(128, 64), kk > 0);
+    tc::mma_commit(&mbar);
+  }
+  // ---- meanwhile: A operands of MMA S in TMEM (rows v / k, K = s), K~^T and Q~
+  chunkc::cp_async_wait_all();
+  __syncthreads();
+  {
+    const int s0 = gh * 32;
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int s = s0 + i;
+      x[i] = s_beta[s] * to_f32(reinterpret_cast<const Tin*>(sm + WS_VST + s * KV_ROW)[l]);
+    }
+    tc::tmem_st32(tq + T_AV + s0, x);
+    float y[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int s = s0 + i;
+      const float kv = to_f32(reinterpret_cast<const Tin*>(sm + WS_KST + s * KV_ROW)[l]) * s_rk[s];
+      x[i] = s_beta[s] * s_eG[s] * kv;
+      y[i] = s_eGC[s] * kv;
+    }
+    tc::tmem_st32(tq + T_AK + s0, x);
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+      chunkc::kst4(rec + R_KT, l, s0 + i, LBO, SBO64, make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]));
+    // Q~ rows: same K-major layout as the q half of the tile, rows scaled
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t off = (tid + WY_THREADS * j) * 16;
+      const int t = (off >> 12) * 8 + ((off & 127) >> 4);
+      const float f = s_rq[t] * s_eG[t];
+      float4 q4 = *reinterpret_cast<const float4*>(sm + WS_XT + 32768 + off);
+      q4.x *= f; q4.y *= f; q4.z *= f; q4.w *= f;
+      *reinterpret_cast<float4*>(rec + R_WQ + 32768 + off) = q4;
+    }
+    tc::tmem_st_wait();
+  }
+  bool ok = tc::mbar_wait(&mbar, 0);
+  if (__syncthreads_or(!ok)) {  // give the MMA one more bounded wait before TMEM goes
+    if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+    tc::mbar_wait(&mbar, 0);
+    goto done;
+  }
+  tc::fence_after_sync();
+
+  // ---- masks: lo rows -> -A (row-major) for the inverse; hi rows -> A_qk
+  {
+    const int t = r64, s0 = gh * 32;
+    float x[32];
+    tc::tmem_ld32(tq + T_D1 + s0, x);
+    const float Gt = s_G[t];
+    if (lo) {
+      const float f = -s_beta[t] * s_rk[t];
+      float* arow = reinterpret_cast<float*>(sm + WS_AAB) + t * RS + s0;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int s = s0 + i;
+        x[i] = s < t ? f * s_rk[s] * __expf(Gt - s_G[s]) * x[i] : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(arow + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+    } else {
+      const float f = s_rq[t];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int s = s0 + i;
+        x[i] = s <= t ? f * s_rk[s] * __expf(Gt - s_G[s]) * x[i] : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        chunkc::kst4(rec + R_AQK, t, s0 + i, LBO, SBO64,
+                     make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
+    }
+  }
+  __syncthreads();
+  chunkc::tri_inverse64(reinterpret_cast<const float*>(sm + WS_AAB),
+                        reinterpret_cast<float*>(sm + WS_TR), sm + WS_TT, tid);
+  sync_tc();
+
+  // ---- MMA S: (beta v)^T T^T = U^T -> D1 ; (beta e^G k^)^T T^T = W^T -> DW
+  if (tid == 0) {
+    const uint32_t t0 = tc::smem_u32(sm + WS_TT);
+    const uint32_t id = tc::idesc_tf32(128, 64);
+    for (int kk = 0; kk < CH / 8; ++kk)
+      tc::mma_tf32_ta(tm + T_D1, tm + T_AV + kk * 8, tc::smem_desc(t0 + kk * KSTEP, LBO, SBO64),
+                      id, kk > 0);
+    for (int kk = 0; kk < CH / 8; ++kk)
+      tc::mma_tf32_ta(tm + T_DW, tm + T_AK + kk * 8, tc::smem_desc(t0 + kk * KSTEP, LBO, SBO64),
+                      id, kk > 0);
+    tc::mma_commit(&mbar);
+  }
+  ok = tc::mbar_wait(&mbar, 1);
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+    tc::mbar_wait(&mbar, 1);
+    goto done;
+  }
+  tc::fence_after_sync();
+  {
+    const int t0 = gh * 32;
+    float x[32];
+    tc::tmem_ld32(tq + T_D1 + t0, x);  // U^T[v = l][t0 + i] -> U[t][v], 128 B per warp and t
+    float* ucol = reinterpret_cast<float*>(rec + R_U) + l;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ucol[(t0 + i) * VD] = x[i];
+    tc::tmem_ld32(tq + T_DW + t0, x);  // W^T[k = l][t0 + i]
+    // lane l of quad m gets W[t0 + 4j + (l & 3)][4m .. 4m+3]: 16-byte stores
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float a[4] = {x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]};
+      const float4 w4 = quad_transpose(a, lane);
+      *reinterpret_cast<float4*>(rec + R_WQ + tc::kmajor_off(t0 + 4 * j + (l & 3), l & ~3, LBO,
+                                                              SBO128)) = w4;
+    }
+    if (tid == 0) *reinterpret_cast<float*>(rec + R_META) = __expf(GC);
+  }
+
+done:
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem_slot, WY_TMEM_COLS);
+}
+
+// ---------------------------------------------------------------- phase 2
+
+constexpr int ST_THREADS = 256;  // two warps per TMEM lane quarter
+constexpr uint32_t SS_A0 = 0, SS_A1 = PART_A, SS_B = 2 * PART_A;
+constexpr uint32_t ST_SMEM = SS_B + PART_B + 1024;
+static_assert(ST_SMEM <= 227 * 1024, "shared memory budget");
+// TMEM: S^T (128 columns), two MMA A accumulators, u^T (A operand of MMA B)
+constexpr uint32_t ST_TMEM_COLS = 512;
+constexpr uint32_t T_S = 0, T_DA0 = 128, T_DA1 = 256, T_U = 384;
+
+template <typename Tin>
+__global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  __shared__ uint64_t mb_a[2], mb_b, mb_m;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int v = (warp & 3) * 32 + lane;  // TMEM lane = value column
+  const int gq = warp >> 2;              // which half of t / k this thread takes
+  const int n = blockIdx.x, hv = blockIdx.y;
+  const int HV = p.HV;
+  int64_t row = n;
+  if (p.ids) {
+    const int32_t id = p.ids[n];
+    if (id < 0 || (int64_t)id >= p.num_slots) {
+      if (tid == 0) report(p.status, WKVM_ERR_SLOT_RANGE);
+      return;
+    }
+    row = id;
+  }
+  const int64_t soff = ((p.src_slots ? row : n) * HV + hv) * (int64_t)(KD * VD);
+  const int64_t doff = ((p.dst_slots ? row : n) * HV + hv) * (int64_t)(KD * VD);
+  int64_t bos, len;
+  if (p.cu) {
+    bos = p.cu[n];
+    len = p.cu[n + 1] - bos;
+  } else {
+    bos = (int64_t)n * p.T;
+    len = p.T;
+  }
+  const int nch = (int)((len + CH - 1) / CH);
+  const int cend = nch < p.w0 + p.W ? nch : p.w0 + p.W;
+  const int cnt = cend - p.w0;
+  const bool same = p.h_src == p.h_dst && soff == doff;
+  if (cnt <= 0) {  // nothing in this window: carry the state over
+    if (p.h_dst && !same)
+      for (int e = tid; e < KD * VD; e += ST_THREADS)
+        p.h_dst[doff + e] = p.h_src ? p.h_src[soff + e] : 0.f;
+    return;
+  }
+  const uint8_t* recs = p.ws + ((int64_t)n * p.W * HV + hv) * (int64_t)REC_BYTES;
+  const int64_t rstride = (int64_t)HV * REC_BYTES;  // between consecutive chunks
+  Tin* __restrict__ go = static_cast<Tin*>(p.o);
+
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_slot, ST_TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(&mb_a[0], 1);
+    tc::mbar_init(&mb_a[1], 1);
+    tc::mbar_init(&mb_b, 1);
+    tc::mbar_init(&mb_m, 1);
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tm = tmem_slot;
+  const uint32_t tq = tc::tmem_addr(tm, (warp & 3) * 32, 0);
+
+  // S^T[v][k] = h[k][v]
+#pragma unroll 1
+  for (int kb = gq * 64; kb < gq * 64 + 64; kb += 32) {
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = p.h_src ? p.h_src[soff + (kb + i) * VD + v] : 0.f;
+    tc::tmem_st32(tq + T_S + kb, x);
+  }
+  tc::tmem_st_wait();
+
+  uint32_t ph_a[2] = {0, 0}, ph_b = 0, ph_m = 0;
+  int pend_a[2] = {0, 0}, pend_b = 0;  // copies issued and not yet waited for
+  auto issue_a = [&](int i) {
+    const int b = i & 1;
+    tc::mbar_expect_tx(&mb_a[b], PART_A);
+    tc::bulk_g2s(sm + (b ? SS_A1 : SS_A0), recs + i * rstride + R_WQ, PART_A, &mb_a[b]);
+  };
+  auto issue_b = [&](int i) {
+    tc::mbar_expect_tx(&mb_b, PART_B);
+    tc::bulk_g2s(sm + SS_B, recs + i * rstride + R_KT, PART_B, &mb_b);
+  };
+  if (tid == 0) {
+    issue_a(0);
+    if (cnt > 1) issue_a(1);
+    issue_b(0);
+  }
+  pend_a[0] = 1;
+  pend_a[1] = cnt > 1;
+  pend_b = 1;
+
+  // O^T of chunk i (accumulator da) -> o rows t in this thread's half. Lane
+  // pairs swap values so that each store writes two adjacent columns: the
+  // even lane takes rows t0 .. t0+15, the odd lane rows t0+16 .. t0+31.
+  auto output = [&](int i, uint32_t da) {
+    const int c = p.w0 + i;
+    const int64_t tok0 = bos + (int64_t)c * CH;
+    const int clen = (len - (int64_t)c * CH) < CH ? (int)(len - (int64_t)c * CH) : CH;
+    const int t0 = gq * 32;
+    float x[32];
+    tc::tmem_ld32(tq + da + 64 + t0, x);
+    const bool odd = lane & 1;
+    Tin* col = go + (tok0 * HV + hv) * VD + (v & ~1);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float mine = odd ? x[j + 16] : x[j];
+      const float give = odd ? x[j] : x[j + 16];
+      const float other = __shfl_xor_sync(0xffffffffu, give, 1);
+      const int t = t0 + j + (odd ? 16 : 0);
+      union { uint32_t u; Tin e[2]; } pk;
+      pk.e[0] = from_f32<Tin>(odd ? other : mine);
+      pk.e[1] = from_f32<Tin>(odd ? mine : other);
+      if (t < clen) *reinterpret_cast<uint32_t*>(col + (int64_t)t * HV * VD) = pk.u;
+    }
+  };
+
+  bool failed = false;
+  bool mma_inflight = false;
+  // every thread waits; the phase advances only on success so that the
+  // failure path below waits for the same phase again
+  auto wait_all = [&](uint64_t* mb, uint32_t& ph) -> bool {
+    const bool ok = tc::mbar_wait(mb, ph);
+    const bool bad = __syncthreads_or(!ok);
+    tc::fence_after_sync();
+    if (bad && tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+    if (!bad) ph ^= 1u;
+    return !bad;
+  };
+
+#pragma unroll 1
+  for (int i = 0; i < cnt; ++i) {
+    const int b = i & 1;
+    const uint32_t da = b ? T_DA1 : T_DA0;
+    if (!wait_all(&mb_a[b], ph_a[b])) { failed = true; break; }
+    pend_a[b] = 0;
+    if (tid == 0) {  // MMA A: S^T x [W; Q~]^T
+      const uint32_t a0 = tc::smem_u32(sm + (b ? SS_A1 : SS_A0));
+      const uint32_t id = tc::idesc_tf32(128, 128);
+      for (int kk = 0; kk < KD / 8; ++kk)
+        tc::mma_tf32_ta(tm + da, tm + T_S + kk * 8, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO128),
+                        id, kk > 0);
+      tc::mma_commit(&mb_m);
+    }
+    mma_inflight = true;
+    if (i > 0) output(i - 1, b ? T_DA0 : T_DA1);  // overlaps MMA A
+    if (!wait_all(&mb_m, ph_m)) { failed = true; break; }
+    mma_inflight = false;
+    if (tid == 0 && i + 2 < cnt) issue_a(i + 2);
+    if (i + 2 < cnt) pend_a[b] = 1;
+    if (!wait_all(&mb_b, ph_b)) { failed = true; break; }
+    pend_b = 0;
+    {  // u^T = U^T - (W S)^T ; S^T *= e^(G_C)
+      const float* ucol = reinterpret_cast<const float*>(sm + SS_B + (R_U - R_KT)) + v;
+      {
+        const int t0 = gq * 32;
+        float x[32];
+        tc::tmem_ld32(tq + da + t0, x);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] = ucol[(t0 + j) * VD] - x[j];
+        tc::tmem_st32(tq + T_U + t0, x);
+      }
+      const float eg = *reinterpret_cast<const float*>(sm + SS_B + (R_META - R_KT));
+#pragma unroll 1
+      for (int kb = gq * 64; kb < gq * 64 + 64; kb += 32) {
+        float x[32];
+        tc::tmem_ld32(tq + T_S + kb, x);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] *= eg;
+        tc::tmem_st32(tq + T_S + kb, x);
+      }
+      tc::tmem_st_wait();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (tid == 0) {  // MMA B: S^T += u^T K~ ; O^T += u^T A_qk^T
+      const uint32_t k0 = tc::smem_u32(sm + SS_B);
+      const uint32_t q0 = k0 + (R_AQK - R_KT);
+      const uint32_t id128 = tc::idesc_tf32(128, 128), id64 = tc::idesc_tf32(128, 64);
+      for (int kk = 0; kk < CH / 8; ++kk)
+        tc::mma_tf32_ta(tm + T_S, tm + T_U + kk * 8, tc::smem_desc(k0 + kk * KSTEP, LBO, SBO64),
+                        id128, true);
+      for (int kk = 0; kk < CH / 8; ++kk)
+        tc::mma_tf32_ta(tm + da + 64, tm + T_U + kk * 8,
+                        tc::smem_desc(q0 + kk * KSTEP, LBO, SBO64), id64, true);
+      tc::mma_commit(&mb_m);
+    }
+    mma_inflight = true;
+    if (!wait_all(&mb_m, ph_m)) { failed = true; break; }
+    mma_inflight = false;
+    if (tid == 0 && i + 1 < cnt) issue_b(i + 1);
+    if (i + 1 < cnt) pend_b = 1;
+  }
+
+  if (!failed) {
+    output(cnt - 1, ((cnt - 1) & 1) ? T_DA1 : T_DA0);
+    if (p.h_dst) {
+#pragma unroll 1
+      for (int kb = gq * 64; kb < gq * 64 + 64; kb += 32) {
+        float x[32];
+        tc::tmem_ld32(tq + T_S + kb, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p.h_dst[doff + (kb + i) * VD + v] = x[i];
+      }
+    }
+  } else {
+    // let copies and MMAs in flight land before the shared memory goes away
+    if (pend_a[0]) tc::mbar_wait(&mb_a[0], ph_a[0]);
+    if (pend_a[1]) tc::mbar_wait(&mb_a[1], ph_a[1]);
+    if (pend_b) tc::mbar_wait(&mb_b, ph_b);
+    if (mma_inflight) tc::mbar_wait(&mb_m, ph_m);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tm, ST_TMEM_COLS);
+}
+
+template <typename Tin>
+int run_windows(const WyArgs& wa0, const int32_t* ids, int64_t num_slots, const float* h_in, float* h_out, bool slots, float* carry,
+                void* o, int nseq, int64_t max_chunks, int64_t W, cudaStream_t stream) {
+  auto k1 = gdn_wy_kernel<Tin>;
+  auto k2 = gdn_state_kernel<Tin>;
+  WKVM_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, WY_SMEM));
+  WKVM_CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, ST_SMEM));
+  // one window: h_in -> h_out directly; several: h_in -> carry -> ... -> h_out
+  const int64_t nwin = max_chunks > 0 ? (max_chunks + W - 1) / W : 1;
+  for (int64_t w = 0; w < nwin; ++w) {
+    WyArgs a = wa0;
+    a.w0 = (int)(w * W);
+    const int64_t wn = max_chunks - a.w0 < W ? max_chunks - a.w0 : W;
+    const bool first = w == 0, final = w == nwin - 1;
+    StateArgs sa{a.ws, o, first ? h_in : carry, final ? h_out : carry, first && slots,
+                 final && slots, ids, num_slots, a.cu, a.T, a.HV, a.w0, (int)W, a.status};
+    if (wn > 0) k1<<<dim3((unsigned)wn, nseq, a.HV), WY_THREADS, WY_SMEM, stream>>>(a);
+    k2<<<dim3(nseq, a.HV), ST_THREADS, ST_SMEM, stream>>>(sa);
+    WKVM_CUDA_TRY(cudaGetLastError());
+  }
+  return WKVM_OK;
+}
+
+}  // namespace
+
+int64_t gdn_two_phase_workspace_bytes(int64_t nseq, int64_t T, int64_t HV) {
+  const int64_t chunks = (T + gdnwy::CH - 1) / gdnwy::CH;
+  return chunks * nseq * HV * (int64_t)gdnwy::REC_BYTES;
+}
+
+// Runs the two-phase prefill when the workspace holds at least one window;
+// returns WKVM_ERR_UNSUPPORTED otherwise (the caller then runs the one-kernel
+// path). h_in / h_out are indexed by slot id when `slots` is set.
+int gdn_two_phase(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                  void* o, const float* h_in, float* h_out, bool slots, const int32_t* ids,
+                  int64_t num_slots, const int64_t* cu, int nseq, int T, int H, int HV,
+                  float scale, bool l2norm, int dtype, void* workspace, int64_t ws_bytes,
+                  int* status, cudaStream_t stream) {
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return WKVM_ERR_UNSUPPORTED;
+  const int64_t max_chunks = (T + CH - 1) / CH;
+  const int64_t per_chunk = (int64_t)nseq * HV * REC_BYTES;
+  const int64_t state_bytes = (int64_t)nseq * HV * KD * VD * 4;
+  int64_t W;
+  uint8_t* recs = static_cast<uint8_t*>(workspace);
+  float* carry = nullptr;
+  if (ws_bytes >= max_chunks * per_chunk) {
+    W = max_chunks > 0 ? max_chunks : 1;
+  } else {
+    const int64_t sb = (state_bytes + 255) & ~int64_t(255);
+    W = (ws_bytes - sb) / per_chunk;
+    if (W < 1) return WKVM_ERR_UNSUPPORTED;
+    carry = reinterpret_cast<float*>(recs);
+    recs += sb;
+  }
+  if (W > max_chunks && max_chunks > 0) W = max_chunks;
+  if (W > 0x7fffffff) return WKVM_ERR_INVALID_ARG;
+  if (nseq > 65535 || HV > 65535) return WKVM_ERR_UNSUPPORTED;
+  WyArgs wa{q, k, v, g, beta, recs, cu, T, H, HV, 0, (int)W, scale, l2norm, status};
+  return dtype == WKVM_DTYPE_BF16
+             ? run_windows<__nv_bfloat16>(wa, ids, num_slots, h_in, h_out, slots, carry, o, nseq,
+                                         max_chunks, W, stream)
+             : run_windows<__half>(wa, ids, num_slots, h_in, h_out, slots, carry, o, nseq,
+                                   max_chunks, W, stream);
+}
+
+}  // namespace wkvm
+
+extern "C" int64_t wkvm_gdn_chunk_workspace_bytes(int32_t nseq, int32_t T, int32_t HV, int32_t K,
+                                                  int32_t V) {
+  if (nseq < 0 || T < 0 || HV <= 0 || K != wkvm::gdnwy::KD || V != wkvm::gdnwy::VD) return 0;
+  return wkvm::gdn_two_phase_workspace_bytes(nseq, T, HV);
+}

@@ -96,6 +96,28 @@ __device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
                : "memory");
 }
 
+// Makes a fresh mbarrier initialisation visible to the async proxy (bulk copies).
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Arrives once on `mbar` and adds `bytes` to the transaction count that the
+// current phase waits for.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               :: "r"(smem_u32(mbar)), "r"(bytes) : "memory");
+}
+
+// Untiled bulk copy global -> this CTA's shared memory (no multicast); both
+// addresses 16-byte aligned, `bytes` a multiple of 16. Completion is counted
+// on `mbar` as transaction bytes.
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes,
+                                         uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      :: "r"(smem_u32(dst_smem)), "l"(src), "r"(bytes), "r"(smem_u32(mbar)) : "memory");
+}
+
 // Waits for phase `parity` of `mbar` to complete with non-blocking polls,
 // giving up after a bounded number of them (well under a second). Returns
 // false on timeout; the caller reports WKVM_ERR_TIMEOUT and winds down.

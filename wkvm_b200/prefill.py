@@ -1,10 +1,12 @@
 """Prefill entry points (chunk_rwkv7 / chunk_gated_delta_rule and their
 slot-native forms).
 
-RWKV-7 (head dim 64) and the GDN sibling (K = V = 128) run fused chunked
-tensor-core kernels (tcgen05 tf32, 64-token chunks, state kept on chip
-across chunks). Other head sizes run the recurrent kernel, which streams the
-state once and loops over tokens.
+RWKV-7 (head dim 64) runs a fused chunked tensor-core kernel (tcgen05 tf32,
+64-token chunks, state kept on chip across chunks). The GDN sibling
+(K = V = 128) runs two launches over a device workspace: a chunk-parallel WY
+kernel, then a sequential pass with the state resident in tensor memory
+(or, with the workspace switched off, one fused kernel). Other head sizes run
+the recurrent kernel, which streams the state once and loops over tokens.
 The initial state comes from ``initial_state`` (or a bank slot) and the final
 state goes to a new tensor (or back into the slot).
 """
@@ -15,6 +17,26 @@ import torch
 
 from . import _lib
 from . import ops as _ops
+
+# Upper bound on the GDN prefill workspace (bytes). Past it the chunks are
+# processed in windows; 0 selects the one-kernel path.
+GDN_WORKSPACE_LIMIT = 2 << 30
+
+
+def _gdn_workspace(nseq, T, HV, K, V, device):
+    """Device workspace for the two-launch GDN prefill, or None."""
+    limit = GDN_WORKSPACE_LIMIT
+    if limit <= 0:
+        return None
+    lib = _lib.load()
+    full = lib.wkvm_gdn_chunk_workspace_bytes(nseq, T, HV, K, V)
+    if full <= 0:
+        return None
+    # one window: carried state + one chunk record per (sequence, head)
+    minimum = nseq * HV * K * V * 4 + 256 + lib.wkvm_gdn_chunk_workspace_bytes(nseq, 1, HV, K, V)
+    size = full if full <= limit else max(limit, minimum)
+    return torch.empty(size, dtype=torch.uint8, device=device)
+
 
 
 def chunk_dplr(r, w, k, v, a, b, scale, initial_state, output_final_state, cu_seqlens):
@@ -35,12 +57,13 @@ def chunk_gdn(q, k, v, g, beta, scale, initial_state, output_final_state, use_qk
     h0 = _ops._state(initial_state)
     o = torch.empty_like(v)
     ht = torch.empty(N, HV, K, V, dtype=torch.float32, device=q.device) if output_final_state else None
+    ws = _gdn_workspace(N, T, HV, K, V, q.device)
     with torch.cuda.device(q.device):
         _lib.call("wkvm_chunk_gated_delta_rule", _ops._ptr(q), _ops._ptr(k), _ops._ptr(v),
                   _ops._ptr(g), _ops._ptr(beta), _ops._ptr(o), _ops._ptr(h0), _ops._ptr(ht),
                   _ops._ptr(cu), N if cu is not None else B, T, H, HV, K, V, float(scale),
-                  int(bool(use_qk_l2norm)), dt, _ops._ptr(_ops.status_word(q.device)),
-                  _ops._stream(q.device))
+                  int(bool(use_qk_l2norm)), dt, _ops._ptr(ws), ws.numel() if ws is not None else 0,
+                  _ops._ptr(_ops.status_word(q.device)), _ops._stream(q.device))
     return o, ht
 
 
@@ -87,10 +110,12 @@ def gdn_prefill_slots(q, k, v, g, beta, bank, layer, slot_ids, scale, use_qk_l2n
         raise ValueError(f"{ids.numel()} slot ids for {nseq} sequences")
     cu = _ops._cu(cu_seqlens, q.device)
     o = torch.empty_like(v) if out is None else out
+    ws = _gdn_workspace(nseq, T, HV, K, V, q.device)
     with torch.cuda.device(q.device):
         _lib.call("wkvm_gdn_prefill_slots", _ops._ptr(q), _ops._ptr(k), _ops._ptr(v),
                   _ops._ptr(g), _ops._ptr(beta), _ops._ptr(o), _ops._ptr(layer_t),
                   layer_t.shape[0], _ops._ptr(ids), _ops._ptr(cu), nseq, T, H, HV, K, V,
-                  float(scale), int(bool(use_qk_l2norm)), dt,
+                  float(scale), int(bool(use_qk_l2norm)), dt, _ops._ptr(ws),
+                  ws.numel() if ws is not None else 0,
                   _ops._ptr(_ops.status_word(q.device)), _ops._stream(q.device))
     return o
