@@ -24,6 +24,8 @@
 // Records live in a caller-provided workspace; when it is smaller than the
 // whole prefill needs, the sequences are processed in windows of chunks and
 // the state is carried between windows in the workspace.
+#include <type_traits>
+
 #include "chunk_common.cuh"
 
 namespace wkvm {
@@ -57,7 +59,7 @@ struct WyArgs {
   const void *q, *k, *v, *g, *beta;
   uint8_t* ws;        // records [nseq][W][HV]
   const int64_t* cu;
-  int T, H, HV, w0, W;
+  int T, H, HV, w0, W, nseq;
   float scale;
   bool l2norm;
   int* status;
@@ -113,24 +115,59 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // ---------------------------------------------------------------- phase 1
 
 constexpr int WY_THREADS = 256;
-// shared memory: [k; q] tile (128 rows x K = 128, unnormalised) = 64 KiB.
-// After MMA 1 the same bytes hold -A (row-major), the inverse's scratch and
-// the T tile.
-constexpr uint32_t WS_XT = 0;
-constexpr uint32_t WS_AAB = 0;
+// Persistent: each CTA works through jobs (chunk, sequence, value head) with a
+// two-stage pipeline; job j+1's inputs land while job j computes.
+// A stage: [k; q] rows as a 16-bit K-major tile (128 rows x K = 128, SBO 2048;
+// the operands of the Gram MMA, copied in place by cp.async) and the v rows
+// (16-bit, row-major, padded). Once the stage's k and v have been read,
+// its first bytes hold -A (row-major), the inverse's scratch and the T tile.
+constexpr uint32_t SBO_H = 2048;                      // 16-bit tile, K = 128
+constexpr uint32_t V_ROW = VD * 2 + 16;
+constexpr uint32_t ST_QK = 0;
+constexpr uint32_t ST_V = ST_QK + 2 * CH * KD * 2;    // 32 KiB
+constexpr uint32_t STAGE = ST_V + CH * V_ROW;         // 50176 B
+constexpr uint32_t WS_AAB = 0;                        // within the job's stage
 constexpr uint32_t WS_TR = WS_AAB + CH * RS * 4;
-constexpr uint32_t WS_TT = 36864;
-static_assert(WS_TR + CH * RS * 4 <= WS_TT, "inverse scratch overlaps the T tile");
-constexpr uint32_t KV_ROW = KD * 2 + 16;           // staged 16-bit k / v row (+16 pad)
-constexpr uint32_t WS_KST = 65536;                  // k rows, 16-bit
-constexpr uint32_t WS_VST = WS_KST + CH * KV_ROW;   // v rows, 16-bit
-constexpr uint32_t WY_SMEM = WS_VST + CH * KV_ROW + 1024;
+constexpr uint32_t WS_TT = WS_AAB;                    // written after -A is spent
+static_assert(WS_TR + CH * RS * 4 <= STAGE, "inverse scratch outside the stage");
+constexpr uint32_t WY_SMEM = 2 * STAGE + 1024;
 // TMEM: MMA 1 accumulator, later U^T | (beta v)^T | (beta e^G k^)^T | W^T
 constexpr uint32_t WY_TMEM_COLS = 256;
 constexpr uint32_t T_D1 = 0, T_AV = 64, T_AK = 128, T_DW = 192;
 
+// Byte offset of element (row, k) of a 16-bit K-major tile with SBO 2048.
+__device__ __forceinline__ uint32_t hoff(int row, int k) {
+  return (row >> 3) * SBO_H + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2;
+}
+
+struct Job {
+  int n, hv, cw;   // sequence, value head, chunk within the window
+  int64_t tok0;
+  int clen;        // tokens in the chunk (0: past the sequence end)
+};
+
+__device__ __forceinline__ Job job_of(const WyArgs& p, int j) {
+  Job J;
+  J.hv = j % p.HV;
+  const int r = j / p.HV;
+  J.n = r % p.nseq;
+  J.cw = r / p.nseq;
+  int64_t bos, len;
+  if (p.cu) {
+    bos = p.cu[J.n];
+    len = p.cu[J.n + 1] - bos;
+  } else {
+    bos = (int64_t)J.n * p.T;
+    len = p.T;
+  }
+  const int64_t rem = len - (int64_t)(p.w0 + J.cw) * CH;
+  J.clen = rem <= 0 ? 0 : (rem < CH ? (int)rem : CH);
+  J.tok0 = bos + (int64_t)(p.w0 + J.cw) * CH;
+  return J;
+}
+
 template <typename Tin>
-__global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p) {
+__global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njobs) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   __shared__ uint64_t mbar;
@@ -142,243 +179,277 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p) {
   const int l = quarter * 32 + lane;  // TMEM lane
   const bool lo = l < 64;
   const int r64 = l & 63;
-  const int n = blockIdx.y, hv = blockIdx.z;
-  const int H = p.H, HV = p.HV, hq = hv / (HV / H);
-  const int c = p.w0 + blockIdx.x;
-  int64_t bos, len;
-  if (p.cu) {
-    bos = p.cu[n];
-    len = p.cu[n + 1] - bos;
-  } else {
-    bos = (int64_t)n * p.T;
-    len = p.T;
-  }
-  if ((int64_t)c * CH >= len) return;  // past this sequence's end (uniform)
-  const int64_t tok0 = bos + (int64_t)c * CH;
-  const int clen = (len - (int64_t)c * CH) < CH ? (int)(len - (int64_t)c * CH) : CH;
-  uint8_t* rec = p.ws + (((int64_t)n * p.W + blockIdx.x) * HV + hv) * (int64_t)REC_BYTES;
+  const int H = p.H, HV = p.HV;
   const Tin* __restrict__ gq = static_cast<const Tin*>(p.q);
   const Tin* __restrict__ gk = static_cast<const Tin*>(p.k);
   const Tin* __restrict__ gv = static_cast<const Tin*>(p.v);
+  const Tin* __restrict__ gg = static_cast<const Tin*>(p.g);
+  const Tin* __restrict__ gb = static_cast<const Tin*>(p.beta);
+  constexpr bool kBf16 = std::is_same<Tin, __nv_bfloat16>::value;
 
   if (warp == 0) {
     tc::tmem_alloc(&tmem_slot, WY_TMEM_COLS);
     tc::tmem_relinquish();
   }
   if (tid == 0) tc::mbar_init(&mbar, 1);
-  {  // k and v rows -> shared memory (read column-wise for the TMEM operands)
-    const uint32_t base = tc::smem_u32(sm);
+
+  // async copies of job J's q, k, v rows into stage st (zeros past clen);
+  // every thread commits one group per call, empty or not
+  auto stage_in = [&](const Job& J, int st) {
+    const uint32_t base = tc::smem_u32(sm + st * STAGE);
+    const int hq = J.hv / (HV / H);
 #pragma unroll
-    for (int j = 0; j < 2 * CH * 16 / WY_THREADS; ++j) {
+    for (int j = 0; j < 3 * CH * 16 / WY_THREADS; ++j) {
       const int e = tid + WY_THREADS * j;
-      const int isv = e >> 10, t = (e >> 4) & 63, piece = e & 15;
-      const uint32_t off = (isv ? WS_VST : WS_KST) + t * KV_ROW + piece * 16;
-      const Tin* src = isv ? gv + ((tok0 + t) * HV + hv) * VD : gk + ((tok0 + t) * H + hq) * KD;
-      if (t < clen) chunkc::cp_async16(base + off, reinterpret_cast<const uint8_t*>(src) + piece * 16);
-      else *reinterpret_cast<uint4*>(sm + off) = make_uint4(0, 0, 0, 0);
+      const int which = e >> 10, t = (e >> 4) & 63, piece = e & 15;  // 0 k, 1 q, 2 v
+      uint32_t off;
+      const Tin* src;
+      if (which < 2) {
+        off = ST_QK + hoff(which * 64 + t, piece * 8);
+        src = (which ? gq : gk) + ((J.tok0 + t) * H + hq) * KD + piece * 8;
+      } else {
+        off = ST_V + t * V_ROW + piece * 16;
+        src = gv + ((J.tok0 + t) * HV + J.hv) * VD + piece * 8;
+      }
+      if (t < J.clen) chunkc::cp_async16(base + off, src);
+      else *reinterpret_cast<uint4*>(sm + st * STAGE + off) = make_uint4(0, 0, 0, 0);
     }
     chunkc::cp_async_commit();
-  }
-  // per-token decay and beta (warp 0; loads issued before the tile loads)
-  float ga = 0.f, gb2 = 0.f, ba = 0.f, bb = 0.f;
-  if (warp == 0) {
-    const Tin* gg = static_cast<const Tin*>(p.g);
-    const Tin* gb = static_cast<const Tin*>(p.beta);
-    if (lane < clen) {
-      ga = to_f32(gg[(tok0 + lane) * HV + hv]);
-      ba = to_f32(gb[(tok0 + lane) * HV + hv]);
-    }
-    if (lane + 32 < clen) {
-      gb2 = to_f32(gg[(tok0 + lane + 32) * HV + hv]);
-      bb = to_f32(gb[(tok0 + lane + 32) * HV + hv]);
-    }
-  }
-  // [k; q] rows -> fp32 K-major tile; squared norms per row
-  {
-    const int r = tid >> 1, half = tid & 1;
-    const int t = r & 63;
-    const bool isq = r >= 64;
-    const bool valid = t < clen;
-    const Tin* src = (isq ? gq : gk) + ((tok0 + t) * H + hq) * KD + half * 64;
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (valid) u = __ldg(reinterpret_cast<const uint4*>(src) + j);
-      const Tin* e = reinterpret_cast<const Tin*>(&u);
-      float x[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        x[i] = to_f32(e[i]);
-        ss = fmaf(x[i], x[i], ss);
+  };
+  // per-token decay and beta of job J into warp 0's registers
+  auto scalars_in = [&](const Job& J, float (&x)[4]) {
+    x[0] = x[1] = x[2] = x[3] = 0.f;
+    if (warp == 0) {
+      if (lane < J.clen) {
+        x[0] = to_f32(gg[(J.tok0 + lane) * HV + J.hv]);
+        x[2] = to_f32(gb[(J.tok0 + lane) * HV + J.hv]);
       }
-      const int k0 = half * 64 + j * 8;
-      chunkc::kst4(sm + WS_XT, r, k0, LBO, SBO128, make_float4(x[0], x[1], x[2], x[3]));
-      chunkc::kst4(sm + WS_XT, r, k0 + 4, LBO, SBO128, make_float4(x[4], x[5], x[6], x[7]));
-    }
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    if (half == 0) {
-      const float f = p.l2norm ? 1.0f / sqrtf(ss + 1e-6f) : 1.f;
-      if (isq) s_rq[t] = f * p.scale;
-      else s_rk[t] = f;
-    }
-  }
-  if (warp == 0) {  // inclusive decay scan
-    float a = ga, b = gb2;
-    s_beta[lane] = ba;
-    s_beta[lane + 32] = bb;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const float ua = __shfl_up_sync(0xffffffffu, a, off);
-      const float ub = __shfl_up_sync(0xffffffffu, b, off);
-      if (lane >= off) {
-        a += ua;
-        b += ub;
+      if (lane + 32 < J.clen) {
+        x[1] = to_f32(gg[(J.tok0 + lane + 32) * HV + J.hv]);
+        x[3] = to_f32(gb[(J.tok0 + lane + 32) * HV + J.hv]);
       }
     }
-    b += __shfl_sync(0xffffffffu, a, 31);
-    const float gc = __shfl_sync(0xffffffffu, b, 31);
-    s_G[lane] = a;
-    s_G[lane + 32] = b;
-    s_eG[lane] = __expf(a);
-    s_eG[lane + 32] = __expf(b);
-    s_eGC[lane] = __expf(gc - a);
-    s_eGC[lane + 32] = __expf(gc - b);
-  }
-  sync_tc();
-  const uint32_t tm = tmem_slot;
-  const uint32_t tq = tc::tmem_addr(tm, quarter * 32, 0);
-  const float GC = s_G[CH - 1];
+  };
 
-  // ---- MMA 1: [k; q] x k^T -> D1 (Gram blocks, unnormalised)
-  if (tid == 0) {
-    const uint32_t x0 = tc::smem_u32(sm + WS_XT);
-    for (int kk = 0; kk < KD / 8; ++kk)
-      tc::mma_tf32(tm + T_D1, tc::smem_desc(x0 + kk * KSTEP, LBO, SBO128),
-                   tc::smem_desc(x0 + kk * KSTEP, LBO, SBO128), tc::idesc_tf32(128, 64), kk > 0);
-    tc::mma_commit(&mbar);
-  }
-  // ---- meanwhile: A operands of MMA S in TMEM (rows v / k, K = s), K~^T and Q~
-  chunkc::cp_async_wait_all();
-  __syncthreads();
-  {
-    const int s0 = gh * 32;
-    float x[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int s = s0 + i;
-      x[i] = s_beta[s] * to_f32(reinterpret_cast<const Tin*>(sm + WS_VST + s * KV_ROW)[l]);
-    }
-    tc::tmem_st32(tq + T_AV + s0, x);
-    float y[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int s = s0 + i;
-      const float kv = to_f32(reinterpret_cast<const Tin*>(sm + WS_KST + s * KV_ROW)[l]) * s_rk[s];
-      x[i] = s_beta[s] * s_eG[s] * kv;
-      y[i] = s_eGC[s] * kv;
-    }
-    tc::tmem_st32(tq + T_AK + s0, x);
-#pragma unroll
-    for (int i = 0; i < 32; i += 4)
-      chunkc::kst4(rec + R_KT, l, s0 + i, LBO, SBO64, make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]));
-    // Q~ rows: same K-major layout as the q half of the tile, rows scaled
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t off = (tid + WY_THREADS * j) * 16;
-      const int t = (off >> 12) * 8 + ((off & 127) >> 4);
-      const float f = s_rq[t] * s_eG[t];
-      float4 q4 = *reinterpret_cast<const float4*>(sm + WS_XT + 32768 + off);
-      q4.x *= f; q4.y *= f; q4.z *= f; q4.w *= f;
-      *reinterpret_cast<float4*>(rec + R_WQ + 32768 + off) = q4;
-    }
-    tc::tmem_st_wait();
-  }
-  bool ok = tc::mbar_wait(&mbar, 0);
-  if (__syncthreads_or(!ok)) {  // give the MMA one more bounded wait before TMEM goes
-    if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
-    tc::mbar_wait(&mbar, 0);
-    goto done;
-  }
-  tc::fence_after_sync();
-
-  // ---- masks: lo rows -> -A (row-major) for the inverse; hi rows -> A_qk
-  {
-    const int t = r64, s0 = gh * 32;
-    float x[32];
-    tc::tmem_ld32(tq + T_D1 + s0, x);
-    const float Gt = s_G[t];
-    if (lo) {
-      const float f = -s_beta[t] * s_rk[t];
-      float* arow = reinterpret_cast<float*>(sm + WS_AAB) + t * RS + s0;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int s = s0 + i;
-        x[i] = s < t ? f * s_rk[s] * __expf(Gt - s_G[s]) * x[i] : 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4*>(arow + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
-    } else {
-      const float f = s_rq[t];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int s = s0 + i;
-        x[i] = s <= t ? f * s_rk[s] * __expf(Gt - s_G[s]) * x[i] : 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        chunkc::kst4(rec + R_AQK, t, s0 + i, LBO, SBO64,
-                     make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
-    }
-  }
-  __syncthreads();
-  chunkc::tri_inverse64(reinterpret_cast<const float*>(sm + WS_AAB),
-                        reinterpret_cast<float*>(sm + WS_TR), sm + WS_TT, tid);
-  sync_tc();
-
-  // ---- MMA S: (beta v)^T T^T = U^T -> D1 ; (beta e^G k^)^T T^T = W^T -> DW
-  if (tid == 0) {
-    const uint32_t t0 = tc::smem_u32(sm + WS_TT);
-    const uint32_t id = tc::idesc_tf32(128, 64);
-    for (int kk = 0; kk < CH / 8; ++kk)
-      tc::mma_tf32_ta(tm + T_D1, tm + T_AV + kk * 8, tc::smem_desc(t0 + kk * KSTEP, LBO, SBO64),
-                      id, kk > 0);
-    for (int kk = 0; kk < CH / 8; ++kk)
-      tc::mma_tf32_ta(tm + T_DW, tm + T_AK + kk * 8, tc::smem_desc(t0 + kk * KSTEP, LBO, SBO64),
-                      id, kk > 0);
-    tc::mma_commit(&mbar);
-  }
-  ok = tc::mbar_wait(&mbar, 1);
-  if (__syncthreads_or(!ok)) {
-    if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
-    tc::mbar_wait(&mbar, 1);
-    goto done;
-  }
-  tc::fence_after_sync();
-  {
-    const int t0 = gh * 32;
-    float x[32];
-    tc::tmem_ld32(tq + T_D1 + t0, x);  // U^T[v = l][t0 + i] -> U[t][v], 128 B per warp and t
-    float* ucol = reinterpret_cast<float*>(rec + R_U) + l;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) ucol[(t0 + i) * VD] = x[i];
-    tc::tmem_ld32(tq + T_DW + t0, x);  // W^T[k = l][t0 + i]
-    // lane l of quad m gets W[t0 + 4j + (l & 3)][4m .. 4m+3]: 16-byte stores
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float a[4] = {x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]};
-      const float4 w4 = quad_transpose(a, lane);
-      *reinterpret_cast<float4*>(rec + R_WQ + tc::kmajor_off(t0 + 4 * j + (l & 3), l & ~3, LBO,
-                                                              SBO128)) = w4;
-    }
-    if (tid == 0) *reinterpret_cast<float*>(rec + R_META) = __expf(GC);
-  }
-
-done:
+  int j = blockIdx.x;
+  Job cur = job_of(p, j < njobs ? j : 0);
+  if (j >= njobs) cur.clen = 0;
+  float sc_cur[4], sc_next[4];
+  stage_in(cur, 0);
+  scalars_in(cur, sc_cur);
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem_slot, WY_TMEM_COLS);
+  tc::fence_after_sync();
+  const uint32_t tm = tmem_slot;
+  const uint32_t tq = tc::tmem_addr(tm, quarter * 32, 0);
+  const uint32_t id_gram = tc::idesc_f16(128, 64, kBf16);
+  const uint32_t id_s = tc::idesc_tf32(128, 64);
+
+#pragma unroll 1
+  for (int it = 0; j < njobs; ++it, j += gridDim.x) {
+    const int st = it & 1;
+    uint8_t* sg = sm + st * STAGE;
+    // prefetch the next job into the other stage (its previous job is done)
+    const int jn = j + gridDim.x;
+    Job nxt = job_of(p, jn < njobs ? jn : 0);
+    if (jn >= njobs) nxt.clen = 0;
+    stage_in(nxt, st ^ 1);
+    scalars_in(nxt, sc_next);
+    const Job J = cur;
+    if (J.clen > 0) {
+      uint8_t* rec = p.ws + (((int64_t)J.n * p.W + J.cw) * HV + J.hv) * (int64_t)REC_BYTES;
+      asm volatile("cp.async.wait_group 1;" ::: "memory");  // this job's stage landed
+      if (warp == 0) {  // inclusive decay scan
+        float a = sc_cur[0], b = sc_cur[1];
+        s_beta[lane] = sc_cur[2];
+        s_beta[lane + 32] = sc_cur[3];
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const float ua = __shfl_up_sync(0xffffffffu, a, off);
+          const float ub = __shfl_up_sync(0xffffffffu, b, off);
+          if (lane >= off) {
+            a += ua;
+            b += ub;
+          }
+        }
+        b += __shfl_sync(0xffffffffu, a, 31);
+        const float gc = __shfl_sync(0xffffffffu, b, 31);
+        s_G[lane] = a;
+        s_G[lane + 32] = b;
+        s_eG[lane] = __expf(a);
+        s_eG[lane + 32] = __expf(b);
+        s_eGC[lane] = __expf(gc - a);
+        s_eGC[lane + 32] = __expf(gc - b);
+      }
+      sync_tc();
+
+      // ---- MMA 1: [k; q] x k^T -> D1 (16-bit operands: the products of
+      //      16-bit inputs are exact in the fp32 accumulator)
+      if (tid == 0) {
+        const uint32_t x0 = tc::smem_u32(sg + ST_QK);
+        for (int kk = 0; kk < KD / 16; ++kk)
+          tc::mma_f16(tm + T_D1, tc::smem_desc(x0 + kk * KSTEP, LBO, SBO_H),
+                      tc::smem_desc(x0 + kk * KSTEP, LBO, SBO_H), id_gram, kk > 0);
+        tc::mma_commit(&mbar);
+      }
+      {  // squared norms per row (thread: half a row)
+        const int r = tid >> 1, half = tid & 1;
+        float ss = 0.f;
+#pragma unroll
+        for (int pc = 0; pc < 8; ++pc) {
+          const uint4 u = *reinterpret_cast<const uint4*>(sg + ST_QK + hoff(r, half * 64 + pc * 8));
+          const Tin* e = reinterpret_cast<const Tin*>(&u);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float x = to_f32(e[i]);
+            ss = fmaf(x, x, ss);
+          }
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        if (half == 0) {
+          const float f = p.l2norm ? 1.0f / sqrtf(ss + 1e-6f) : 1.f;
+          if (r >= 64) s_rq[r - 64] = f * p.scale;
+          else s_rk[r] = f;
+        }
+      }
+      __syncthreads();
+      const float GC = s_G[CH - 1];
+      {  // A operands of MMA S in TMEM (rows v / k, K = s), K~^T and Q~
+        const int s0 = gh * 32;
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int s = s0 + i;
+          x[i] = s_beta[s] * to_f32(reinterpret_cast<const Tin*>(sg + ST_V + s * V_ROW)[l]);
+        }
+        tc::tmem_st32(tq + T_AV + s0, x);
+        float y[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int s = s0 + i;
+          const float kv =
+              to_f32(*reinterpret_cast<const Tin*>(sg + ST_QK + hoff(s, l))) * s_rk[s];
+          x[i] = s_beta[s] * s_eG[s] * kv;
+          y[i] = s_eGC[s] * kv;
+        }
+        tc::tmem_st32(tq + T_AK + s0, x);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          chunkc::kst4(rec + R_KT, l, s0 + i, LBO, SBO64,
+                       make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]));
+        // Q~ (fp32 K-major, rows 64..127 of [W; Q~]): piece e -> row t = 8 g + (e & 7),
+        // 8 columns from (e >> 3) & 15; eight lanes fill 128 contiguous bytes
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int e = tid + WY_THREADS * jj;
+          const int t = (e >> 7) * 8 + (e & 7), k8 = ((e >> 3) & 15) * 8;
+          const uint4 u = *reinterpret_cast<const uint4*>(sg + ST_QK + hoff(64 + t, k8));
+          const Tin* h = reinterpret_cast<const Tin*>(&u);
+          const float f = s_rq[t] * s_eG[t];
+          uint8_t* dst = rec + R_WQ + 32768;
+          chunkc::kst4(dst, t, k8, LBO, SBO128,
+                       make_float4(to_f32(h[0]) * f, to_f32(h[1]) * f, to_f32(h[2]) * f,
+                                   to_f32(h[3]) * f));
+          chunkc::kst4(dst, t, k8 + 4, LBO, SBO128,
+                       make_float4(to_f32(h[4]) * f, to_f32(h[5]) * f, to_f32(h[6]) * f,
+                                   to_f32(h[7]) * f));
+        }
+        tc::tmem_st_wait();
+      }
+      bool ok = tc::mbar_wait(&mbar, 0);
+      if (__syncthreads_or(!ok)) {  // give the MMA one more bounded wait before TMEM goes
+        if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+        tc::mbar_wait(&mbar, 0);
+        break;
+      }
+      tc::fence_after_sync();
+
+      // ---- masks: lo rows -> -A (row-major, over the spent stage) for the
+      //      inverse; hi rows -> A_qk
+      {
+        const int t = r64, s0 = gh * 32;
+        float x[32];
+        tc::tmem_ld32(tq + T_D1 + s0, x);
+        const float Gt = s_G[t];
+        if (lo) {
+          const float f = -s_beta[t] * s_rk[t];
+          float* arow = reinterpret_cast<float*>(sg + WS_AAB) + t * RS + s0;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int s = s0 + i;
+            x[i] = s < t ? f * s_rk[s] * __expf(Gt - s_G[s]) * x[i] : 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(arow + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+        } else {
+          const float f = s_rq[t];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int s = s0 + i;
+            x[i] = s <= t ? f * s_rk[s] * __expf(Gt - s_G[s]) * x[i] : 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            chunkc::kst4(rec + R_AQK, t, s0 + i, LBO, SBO64,
+                         make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
+        }
+      }
+      __syncthreads();
+      chunkc::tri_inverse64(reinterpret_cast<const float*>(sg + WS_AAB),
+                            reinterpret_cast<float*>(sg + WS_TR), sg + WS_TT, tid);
+      sync_tc();
+
+      // ---- MMA S: (beta v)^T T^T = U^T -> D1 ; (beta e^G k^)^T T^T = W^T -> DW
+      if (tid == 0) {
+        const uint32_t t0 = tc::smem_u32(sg + WS_TT);
+        for (int kk = 0; kk < CH / 8; ++kk)
+          tc::mma_tf32_ta(tm + T_D1, tm + T_AV + kk * 8, tc::smem_desc(t0 + kk * KSTEP, LBO, SBO64),
+                          id_s, kk > 0);
+        for (int kk = 0; kk < CH / 8; ++kk)
+          tc::mma_tf32_ta(tm + T_DW, tm + T_AK + kk * 8, tc::smem_desc(t0 + kk * KSTEP, LBO, SBO64),
+                          id_s, kk > 0);
+        tc::mma_commit(&mbar);
+      }
+      ok = tc::mbar_wait(&mbar, 1);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+        tc::mbar_wait(&mbar, 1);
+        break;
+      }
+      tc::fence_after_sync();
+      {
+        const int t0 = gh * 32;
+        float x[32];
+        tc::tmem_ld32(tq + T_D1 + t0, x);  // U^T[v = l][t0 + i] -> U[t][v], 128 B per warp and t
+        float* ucol = reinterpret_cast<float*>(rec + R_U) + l;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ucol[(t0 + i) * VD] = x[i];
+        tc::tmem_ld32(tq + T_DW + t0, x);  // W^T[k = l][t0 + i]
+        // lane l of quad m gets W[t0 + 4j + (l & 3)][4m .. 4m+3]: 16-byte stores
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const float a[4] = {x[4 * jj], x[4 * jj + 1], x[4 * jj + 2], x[4 * jj + 3]};
+          const float4 w4 = quad_transpose(a, lane);
+          *reinterpret_cast<float4*>(rec + R_WQ + tc::kmajor_off(t0 + 4 * jj + (l & 3), l & ~3, LBO,
+                                                                  SBO128)) = w4;
+        }
+        if (tid == 0) *reinterpret_cast<float*>(rec + R_META) = __expf(GC);
+      }
+      // the next job overwrites this stage only after every thread is past here
+      tc::fence_before_sync();
+      __syncthreads();
+      tc::fence_after_sync();
+    }
+    cur = nxt;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sc_cur[i] = sc_next[i];
+  }
+
+  chunkc::cp_async_wait_all();
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tm, WY_TMEM_COLS);
 }
 
 // ---------------------------------------------------------------- phase 2
@@ -510,10 +581,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
 
   bool failed = false;
   bool mma_inflight = false;
-  // every thread waits; the phase advances only on success so that the
-  // failure path below waits for the same phase again
+  // warp 0 polls, the CTA then meets at a barrier; the phase advances only on
+  // success so that the failure path below waits for the same phase again
   auto wait_all = [&](uint64_t* mb, uint32_t& ph) -> bool {
-    const bool ok = tc::mbar_wait(mb, ph);
+    const bool ok = warp != 0 || tc::mbar_wait(mb, ph);
     const bool bad = __syncthreads_or(!ok);
     tc::fence_after_sync();
     if (bad && tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
@@ -539,7 +610,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     if (i > 0) output(i - 1, b ? T_DA0 : T_DA1);  // overlaps MMA A
     if (!wait_all(&mb_m, ph_m)) { failed = true; break; }
     mma_inflight = false;
-    if (tid == 0 && i + 2 < cnt) issue_a(i + 2);
+    if (tid == 0 && i + 2 < cnt) issue_a(i + 2);  // MMA A has read this buffer
     if (i + 2 < cnt) pend_a[b] = 1;
     if (!wait_all(&mb_b, ph_b)) { failed = true; break; }
     pend_b = 0;
@@ -582,7 +653,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     mma_inflight = true;
     if (!wait_all(&mb_m, ph_m)) { failed = true; break; }
     mma_inflight = false;
-    if (tid == 0 && i + 1 < cnt) issue_b(i + 1);
+    if (tid == 0 && i + 1 < cnt) issue_b(i + 1);  // MMA B has read this buffer
     if (i + 1 < cnt) pend_b = 1;
   }
 
@@ -614,6 +685,9 @@ int run_windows(const WyArgs& wa0, const int32_t* ids, int64_t num_slots, const 
                 void* o, int nseq, int64_t max_chunks, int64_t W, cudaStream_t stream) {
   auto k1 = gdn_wy_kernel<Tin>;
   auto k2 = gdn_state_kernel<Tin>;
+  int dev = 0, num_sms = 148;
+  WKVM_CUDA_TRY(cudaGetDevice(&dev));
+  WKVM_CUDA_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
   WKVM_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, WY_SMEM));
   WKVM_CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, ST_SMEM));
   // one window: h_in -> h_out directly; several: h_in -> carry -> ... -> h_out
@@ -625,7 +699,11 @@ int run_windows(const WyArgs& wa0, const int32_t* ids, int64_t num_slots, const 
     const bool first = w == 0, final = w == nwin - 1;
     StateArgs sa{a.ws, o, first ? h_in : carry, final ? h_out : carry, first && slots,
                  final && slots, ids, num_slots, a.cu, a.T, a.HV, a.w0, (int)W, a.status};
-    if (wn > 0) k1<<<dim3((unsigned)wn, nseq, a.HV), WY_THREADS, WY_SMEM, stream>>>(a);
+    if (wn > 0) {
+      const int njobs = (int)(wn * nseq * a.HV);
+      const int grid = njobs < 2 * num_sms ? njobs : 2 * num_sms;
+      k1<<<grid, WY_THREADS, WY_SMEM, stream>>>(a, njobs);
+    }
     k2<<<dim3(nseq, a.HV), ST_THREADS, ST_SMEM, stream>>>(sa);
     WKVM_CUDA_TRY(cudaGetLastError());
   }
@@ -664,9 +742,10 @@ int gdn_two_phase(const void* q, const void* k, const void* v, const void* g, co
     recs += sb;
   }
   if (W > max_chunks && max_chunks > 0) W = max_chunks;
-  if (W > 0x7fffffff) return WKVM_ERR_INVALID_ARG;
+  if (W * nseq * HV > 0x7fffffff) W = 0x7fffffff / ((int64_t)nseq * HV);
+  if (W < 1) return WKVM_ERR_UNSUPPORTED;
   if (nseq > 65535 || HV > 65535) return WKVM_ERR_UNSUPPORTED;
-  WyArgs wa{q, k, v, g, beta, recs, cu, T, H, HV, 0, (int)W, scale, l2norm, status};
+  WyArgs wa{q, k, v, g, beta, recs, cu, T, H, HV, 0, (int)W, nseq, scale, l2norm, status};
   return dtype == WKVM_DTYPE_BF16
              ? run_windows<__nv_bfloat16>(wa, ids, num_slots, h_in, h_out, slots, carry, o, nseq,
                                          max_chunks, W, stream)
