@@ -48,7 +48,8 @@ enum {
   WKVM_ERR_CUDA = -6,         /* a CUDA runtime call failed */
   WKVM_ERR_ALIGN = -7,        /* pointer or row size not 16-byte aligned */
   WKVM_ERR_UNSUPPORTED = -8,  /* option not implemented */
-  WKVM_ERR_TIMEOUT = -9       /* bounded wait ran out */
+  WKVM_ERR_TIMEOUT = -9,      /* bounded wait ran out */
+  WKVM_ERR_SCRATCH = -10      /* request larger than a static scratch array */
 };
 
 enum { WKVM_DTYPE_F32 = 0, WKVM_DTYPE_BF16 = 1, WKVM_DTYPE_F16 = 2 };
@@ -233,6 +234,29 @@ int wkvm_chunk_gated_delta_rule(
  * nseq*HV*(64 KiB + one chunk record) bytes) processes the chunks in
  * windows. */
 int64_t wkvm_gdn_chunk_workspace_bytes(int32_t nseq, int32_t T, int32_t HV, int32_t K, int32_t V);
+
+/* wkvm_chunk_gated_delta_rule for callers that cannot allocate device
+ * memory (a host whose device memory belongs to its own pool, or a cgo / JNI
+ * embedding with no allocator, where cudaMalloc would also synchronise the
+ * device mid-serving). No counterpart exists in the reference: it is the
+ * two-launch path with its workspace in a 64 MiB array that the library
+ * keeps on every GPU that loads it, until the process exits. Arguments as
+ * for wkvm_chunk_gated_delta_rule without the workspace; K == V == 128 and
+ * 16-bit inputs only (WKVM_ERR_SHAPE / WKVM_ERR_DTYPE otherwise). Longer
+ * inputs run in windows of chunks; WKVM_ERR_SCRATCH when even one window
+ * does not fit (about nseq * HV > 300). Runs on the current device; the
+ * first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU (other
+ * streams, other host threads) race; sequential calls need nothing cleared
+ * between them, since each call writes every byte it reads. */
+int wkvm_chunk_gated_delta_rule_static(
+    const void* q, const void* k, const void* v, const void* g,
+    const void* beta, void* o,
+    const float* h0, float* ht, const int64_t* cu_seqlens,
+    int32_t B, int32_t T, int32_t H, int32_t HV, int32_t K, int32_t V,
+    float scale, int32_t use_qk_l2norm, int32_t dtype,
+    int32_t* status, wkvm_stream_t stream);
 
 /* Slot-native chunked GDN prefill: initial and final state of sequence i
  * in bank_layer[slot_ids[i]] ([num_slots, HV, K, V] fp32). No wkvm caller

@@ -45,6 +45,7 @@ SIGNATURES: dict[str, list] = {
     "wkvm_chunk_gated_delta_rule": [P] * 6 + [P, P, P] + [I32] * 6 + [F32, I32, I32, P, I64, P, P],
     "wkvm_gdn_prefill_slots": [P] * 6 + [P, I64, P, P] + [I32] * 6 + [F32, I32, I32, P, I64, P, P],
     "wkvm_gdn_chunk_workspace_bytes": [I32] * 5,
+    "wkvm_chunk_gated_delta_rule_static": [P] * 6 + [P, P, P] + [I32] * 6 + [F32, I32, I32, P, P],
 }
 
 RESTYPES = {
@@ -56,6 +57,7 @@ ERR_NAMES = {
     -1: "WKVM_ERR_INVALID_ARG", -2: "WKVM_ERR_SHAPE", -3: "WKVM_ERR_DTYPE",
     -4: "WKVM_ERR_SLOT_RANGE", -5: "WKVM_ERR_DUPLICATE", -6: "WKVM_ERR_CUDA",
     -7: "WKVM_ERR_ALIGN", -8: "WKVM_ERR_UNSUPPORTED", -9: "WKVM_ERR_TIMEOUT",
+    -10: "WKVM_ERR_SCRATCH",
 }
 
 _lock = threading.Lock()

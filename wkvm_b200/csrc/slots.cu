@@ -256,6 +256,7 @@ extern "C" const char* wkvm_strerror(int code) {
     case WKVM_ERR_ALIGN: return "pointer or size not 16-byte aligned";
     case WKVM_ERR_UNSUPPORTED: return "unsupported option";
     case WKVM_ERR_TIMEOUT: return "bounded wait timed out";
+    case WKVM_ERR_SCRATCH: return "request larger than the static scratch array";
     default: return "unknown error";
   }
 }
