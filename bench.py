@@ -384,7 +384,7 @@ def run_gdn(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     decode = args.workload == "gdn-decode"
-    B, T, HG, K = (512, 1, 16, 128) if decode else (4, 8192, 16, 128)
+    B, T, HG, K = (512, 1, 16, 128) if decode else (args.gdn_batch, 8192, 16, 128)
     bank = torch.empty(1, B + 1, HG, K, K, device=dev)
     bank.normal_(0.0, 0.1, generator=torch.Generator(device=dev).manual_seed(11 + rank))
     ids = ops.slot_ids_tensor(list(range(1, B + 1)), B + 1, dev)
@@ -435,7 +435,11 @@ def run_gdn(args, world, rank, local):
                      "tensor_tflops": round(th * 183e3 / (step_ms * 1e-3) / 1e12, 2),
                      "tensor_peak_tflops": d.get("bf16_tflops", 1590.0) / 2,
                      "tensor_peak_kind": "measured bf16_tflops / 2 (tf32 dense rate)"}
-        kernel = "gdn_chunk_kernel (tcgen05 kind::tf32)"
+        from wkvm_b200 import _lib
+        line_roof["workspace_bytes_per_step"] = int(
+            _lib.load().wkvm_gdn_chunk_workspace_bytes(B, T, HG, K, K))
+        kernel = ("gdn_wy_kernel (chunk-parallel WY, tcgen05 kind::f16 + kind::tf32) -> "
+                  "gdn_state_kernel (sequential state pass, tcgen05 kind::tf32)")
     return {
         "metric": f"GDN {'decode' if decode else 'chunked prefill'} tokens/s (BASELINE config 3)",
         "value": round(world * B * T * args.steps / (ms * 1e-3), 1), "unit": "tokens/s",
@@ -445,7 +449,8 @@ def run_gdn(args, world, rank, local):
         "data": "synthetic (seeded, reference op-level distributions)",
         "config": {"workload": f"B={B} T={T} H=16 K=V=128, state in arena slots",
                    "kernel": kernel},
-        "roofline": line_roof, "clocks": clk.summary(), "gpu_launches": args.steps,
+        "roofline": line_roof, "clocks": clk.summary(),
+        "gpu_launches": args.steps * (1 if decode else 2),
     }
 
 
@@ -664,6 +669,8 @@ def main():
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "gdn-decode", "gdn-prefill", "model-decode"])
     ap.add_argument("--prefill-batch", type=int, default=16)
+    ap.add_argument("--gdn-batch", type=int, default=4,
+                    help="sequences of the gdn-prefill workload (config 3: 4)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
