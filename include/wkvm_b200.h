@@ -117,6 +117,24 @@ int wkvm_wkv7_decode_slots(
  * No counterpart in the reference. */
 int wkvm_set_decode_overlap(int32_t enable);
 
+/* Token-shift + lerp prologue of RWKV-7 single-token decode, with the
+ * token-shift state read and written in place by slot id. For row b
+ * (slot s = slot_ids[b]) and channel d: delta = shift[s][d] - x[b][d]
+ * (rounded to the input dtype, as fla's token_shift stores it),
+ * out[i][b][d] = x[b][d] + delta * mixes[i][d] for i < n_mix (n_mix <= 6),
+ * then shift[s][d] = x[b][d]. x is [B, D], out [n_mix, B, D], each mix [D],
+ * slot rows slot_stride bytes apart (bank.shift[layer, family] rows).
+ * Replaces fla token_shift with a cache (fla/modules/token_shift.py:521) +
+ * torch_addcmul_rwkv7 (fla/ops/rwkv7/fused_addcmul.py:290) in RWKV7Attention,
+ * the same pair with x_k in RWKV7FeedForward
+ * (fla/models/rwkv7/modeling_rwkv7.py:98-115), and wkvm's gather/scatter of
+ * the shift family (wkvm/runner/state.py:63-97). bf16/fp16, D % 8 == 0. */
+int wkvm_wkv7_shift_mix_slots(
+    const void* x, void* out, void* shift_rows, int64_t slot_stride,
+    int64_t num_slots, const int32_t* slot_ids, const void* const* mixes,
+    int32_t n_mix, int32_t B, int32_t D, int32_t dtype,
+    int32_t* status, wkvm_stream_t stream);
+
 /* Fused RWKV-7 time-mix decode core: the whole of fla RWKV7Attention between
  * its projections and o_proj for one token, around an in-place slot update
  * (fla/layers/rwkv7.py:270-349): w = -0.6065306597126334 sigmoid(w_raw),

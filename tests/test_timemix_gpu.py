@@ -64,7 +64,37 @@ def test_timemix_matches_formula_chain(cuda, dtype, first_layer):
         assert_out_close(o, ref)
 
 
-def test_fused_time_mix_model_decode_close_to_fla(cuda):
+@pytest.mark.parametrize("n_mix", [6, 1])
+def test_shift_mix_matches_token_shift_addcmul(cuda, n_mix):
+    # fla decode prologue: delta = token_shift(x, cache) stored as bf16, then
+    # torch.addcmul(x, delta, mix) per mix; the new shift state is x
+    torch.manual_seed(3)
+    L, S, B, D = 2, 9, 5, 256
+    shift = torch.randn(L, 2, S + 1, D, device=cuda).to(torch.bfloat16)
+    before = shift.clone()
+    x = torch.randn(B, 1, D, device=cuda).to(torch.bfloat16)
+    mixes = [torch.rand(1, 1, D, device=cuda).to(torch.bfloat16) for _ in range(n_mix)]
+    ids = [7, 2, 9, 0, 4]
+    layer, fam = 1, n_mix == 1
+    prev = shift[layer, int(fam), ids].view(B, 1, D)
+    delta = (prev.float() - x.float()).to(torch.bfloat16)
+    ref = [torch.addcmul(x, delta, m) for m in mixes]
+    outs = ops.wkv7_shift_mix_slots(x, mixes, shift[layer, int(fam)], ids)
+    ops.check_device_status(cuda)
+    assert len(outs) == n_mix
+    for o, r in zip(outs, ref):
+        assert o.shape == (B, 1, D)
+        # one bf16 rounding of the same fp32 value (at most one ulp apart)
+        assert ((o.float() - r.float()).abs() <= r.float().abs() * 2.0 ** -7 + 1e-30).all()
+    assert torch.equal(shift[layer, int(fam), ids], x.view(B, D))
+    rest = [i for i in range(S + 1) if i not in ids]
+    assert torch.equal(shift[layer, int(fam), rest], before[layer, int(fam), rest])
+    assert torch.equal(shift[layer, 1 - int(fam)], before[layer, 1 - int(fam)])
+    assert torch.equal(shift[0], before[0])
+
+
+@pytest.mark.parametrize("shift_in_bank", [False, True])
+def test_fused_time_mix_model_decode_close_to_fla(cuda, shift_in_bank):
     fla_models = pytest.importorskip("fla.models.rwkv7")
     from fla.models.utils import Cache
     from wkvm_b200 import fla_compat
@@ -83,6 +113,8 @@ def test_fused_time_mix_model_decode_close_to_fla(cuda):
     ref = RWKV7StateBank(lay, num_slots=4, device=cuda)
     for b in (ours, ref):
         b.wkv.copy_(torch.randn_like(b.wkv, generator=torch.Generator(device=cuda).manual_seed(3)) * 0.1)
+        b.shift.copy_(torch.randn(b.shift.shape, device=cuda,
+                                  generator=torch.Generator(device=cuda).manual_seed(4)))
     slots = [2, 4, 1]
     ids = torch.tensor(slots, device=cuda)
     tok = torch.randint(0, 512, (3, 1), device=cuda)
@@ -107,7 +139,7 @@ def test_fused_time_mix_model_decode_close_to_fla(cuda):
         try:
             our_logits = []
             for _ in range(4):
-                h = fla_compat.slot_cache(ours, slots)
+                h = fla_compat.slot_cache(ours, slots, shift_in_bank=shift_in_bank)
                 our_logits.append(model(input_ids=tok, past_key_values=h.cache, use_cache=True,
                                         logits_to_keep=1).logits.float())
                 h.commit()
@@ -117,3 +149,6 @@ def test_fused_time_mix_model_decode_close_to_fla(cuda):
     for o, r in zip(our_logits, ref_logits):
         assert rel_err(o, r) < 3e-2
     assert rel_err(ours.wkv[:, slots], ref.wkv[:, slots]) < 3e-2
+    assert rel_err(ours.shift[:, :, slots], ref.shift[:, :, slots]) < 3e-2
+    rest = [i for i in range(5) if i not in slots]
+    assert torch.equal(ours.shift[:, :, rest], ref.shift[:, :, rest])

@@ -45,6 +45,7 @@ SIGNATURES: dict[str, list] = {
     "wkvm_chunk_gated_delta_rule": [P] * 6 + [P, P, P] + [I32] * 6 + [F32, I32, I32, P, I64, P, P],
     "wkvm_gdn_prefill_slots": [P] * 6 + [P, I64, P, P] + [I32] * 6 + [F32, I32, I32, P, I64, P, P],
     "wkvm_gdn_chunk_workspace_bytes": [I32] * 5,
+    "wkvm_wkv7_shift_mix_slots": [P, P, P, I64, I64, P, P, I32, I32, I32, I32, P, P],
     "wkvm_chunk_gated_delta_rule_static": [P] * 6 + [P, P, P] + [I32] * 6 + [F32, I32, I32, P, P],
 }
 

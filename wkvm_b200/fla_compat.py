@@ -10,8 +10,13 @@ Two levels of drop-in:
   SlotState instead of a gathered copy; the installed ops see it and update
   ``bank.wkv[layer, slot_ids]`` in place, so wkvm's gather_cache /
   scatter_cache copies of the wkv family (wkvm/runner/state.py:63-97)
-  disappear. The token-shift family still travels through the cache, moved
-  with one slot-snapshot kernel for all layers and one restore.
+  disappear. The token-shift family travels through the cache, moved with one
+  gather kernel for all layers and one restore per layer, unless the cache is
+  built with ``shift_in_bank=True`` (single-token decode with
+  ``install(fuse_time_mix=True)``): then each layer gets :class:`SlotShift`
+  markers and the token shift + lerp prologue of both the time-mix and the
+  channel-mix block reads and writes ``bank.shift[layer, family, slot_ids]``
+  in place (ops.wkv7_shift_mix_slots), so nothing is gathered or restored.
 """
 
 from __future__ import annotations
@@ -38,6 +43,25 @@ class SlotState:
     @property
     def device(self) -> torch.device:
         return self.bank_wkv.device
+
+
+@dataclass
+class SlotShift:
+    """One layer's token-shift row family living in the arena:
+    bank_shift[layer, family, ids] (family 0: time mix, 1: channel mix)."""
+
+    bank_shift: torch.Tensor
+    layer: int
+    family: int
+    ids: torch.Tensor  # int32, on the bank's device
+
+    @property
+    def device(self) -> torch.device:
+        return self.bank_shift.device
+
+    @property
+    def rows(self) -> torch.Tensor:
+        return self.bank_shift[self.layer, self.family]
 
 
 def fused_mul_recurrent_rwkv7(r, w, k, v, kk, a, scale: float = 1.0, initial_state=None,
@@ -94,10 +118,18 @@ def _fused_time_mix_forward(self, hidden_states, attention_mask=None, past_key_v
             or cu_seqlens is not None or self.training or not self.fuse_norm):
         return orig(self, hidden_states, attention_mask, past_key_values, use_cache,
                     output_attentions, v_first, cu_seqlens, **kwargs)
-    delta, conv_state = layer.token_shift(hidden_states, cu_seqlens, output_cache=True,
-                                          cache=last["conv_state"])
-    xr, xw, xk, xv, xa, xg = layer.fused_addcmul_rwkv7(hidden_states, delta, self.x_r, self.x_w,
-                                                       self.x_k, self.x_v, self.x_a, self.x_g)
+    shift = last["conv_state"]
+    if isinstance(shift, SlotShift):  # token shift + lerp on the arena rows, in place
+        xr, xw, xk, xv, xa, xg = ops.wkv7_shift_mix_slots(
+            hidden_states, (self.x_r, self.x_w, self.x_k, self.x_v, self.x_a, self.x_g),
+            shift.rows, shift.ids)
+        conv_state = shift
+    else:
+        delta, conv_state = layer.token_shift(hidden_states, cu_seqlens, output_cache=True,
+                                              cache=shift)
+        xr, xw, xk, xv, xa, xg = layer.fused_addcmul_rwkv7(hidden_states, delta, self.x_r,
+                                                           self.x_w, self.x_k, self.x_v,
+                                                           self.x_a, self.x_g)
     r = self.r_proj(xr)
     w_raw = self.w_lora(xw)
     k = self.k_proj(xk)
@@ -116,27 +148,50 @@ def _fused_time_mix_forward(self, hidden_states, attention_mask=None, past_key_v
     return self.o_proj(o), None, past_key_values, v_first
 
 
+def _ffn_forward(self, x, attention_mask=None, state=None, cu_seqlens=None, **kwargs):
+    """RWKV7FeedForward.forward with the token shift + lerp on the arena rows
+    when the cache carries a SlotShift (single-token decode); otherwise
+    fla's own forward."""
+    st = None
+    if state is not None and len(state) > self.layer_idx:
+        st = state[self.layer_idx].get("ffn_state")
+    if (not isinstance(st, SlotShift) or x.shape[1] != 1 or attention_mask is not None
+            or cu_seqlens is not None or self.training):
+        return _orig["ffn_forward"](self, x, attention_mask, state, cu_seqlens, **kwargs)
+    (xk,) = ops.wkv7_shift_mix_slots(x, (self.x_k,), st.rows, st.ids)
+    return self.value(self.act_fn(self.key(xk))), state
+
+
 def install(fuse_time_mix: bool = False) -> None:
     """Points fla's RWKV7Attention at wkvm_b200's WKV ops (idempotent). With
     ``fuse_time_mix`` single-token decode with slot-resident state also runs
-    the gates, norms and output correction inside the decode kernel."""
+    the gates, norms and output correction inside the decode kernel, and the
+    token shift + lerp of both blocks on the arena rows when the cache was
+    built with ``shift_in_bank=True``."""
     import fla.layers.rwkv7 as layer
+    import fla.models.rwkv7.modeling_rwkv7 as modeling
     if not _orig:
         _orig["fused_mul_recurrent_rwkv7"] = layer.fused_mul_recurrent_rwkv7
         _orig["chunk_rwkv7"] = layer.chunk_rwkv7
         _orig["forward"] = layer.RWKV7Attention.forward
+        _orig["ffn_forward"] = modeling.RWKV7FeedForward.forward
     layer.fused_mul_recurrent_rwkv7 = fused_mul_recurrent_rwkv7
     layer.chunk_rwkv7 = chunk_rwkv7
     layer.RWKV7Attention.forward = (_fused_time_mix_forward if fuse_time_mix
                                     else _orig["forward"])
+    modeling.RWKV7FeedForward.forward = (_ffn_forward if fuse_time_mix
+                                         else _orig["ffn_forward"])
 
 
 def uninstall() -> None:
     """Restores fla's own ops and forward."""
     import fla.layers.rwkv7 as layer
+    import fla.models.rwkv7.modeling_rwkv7 as modeling
     for name, fn in _orig.items():
         if name == "forward":
             layer.RWKV7Attention.forward = fn
+        elif name == "ffn_forward":
+            modeling.RWKV7FeedForward.forward = fn
         else:
             setattr(layer, name, fn)
     _orig.clear()
@@ -147,13 +202,23 @@ class SlotCacheHandle:
     rows gathered for this batch; :meth:`commit` writes the updated
     token-shift rows back to the bank."""
 
-    def __init__(self, bank, slot_ids):
+    def __init__(self, bank, slot_ids, shift_in_bank: bool = False):
         from fla.models.utils import Cache
 
         self.bank = bank
         dev = bank.device
         self.ids = ops.slot_ids_tensor(slot_ids, bank.num_slots + 1, dev)
         L = bank.layout.n_layer
+        self.shift_in_bank = shift_in_bank
+        if shift_in_bank:  # the fused prologues read and write bank.shift in place
+            self.shift = None
+            self.cache = Cache()
+            for i in range(L):
+                self.cache.update(recurrent_state=SlotState(bank.wkv, i, self.ids),
+                                  conv_state=SlotShift(bank.shift, i, 0, self.ids),
+                                  ffn_state=SlotShift(bank.shift, i, 1, self.ids),
+                                  layer_idx=i, offset=0)
+            return
         # [L, 2, n, D]: one kernel, and every (layer, family) view is contiguous
         self.shift = ops.slot_gather_outer_major(bank.shift, 2, self.ids)
         self.cache = Cache()
@@ -163,7 +228,10 @@ class SlotCacheHandle:
                               layer_idx=i, offset=0)
 
     def commit(self) -> None:
-        """Writes each layer's new token-shift rows back to the bank."""
+        """Writes each layer's new token-shift rows back to the bank (nothing
+        to do when they were updated in place)."""
+        if self.shift_in_bank:
+            return
         L = self.bank.layout.n_layer
         for i in range(L):
             st = self.cache[i]
@@ -175,5 +243,8 @@ class SlotCacheHandle:
                                  x.reshape(self.ids.numel(), -1).to(self.bank.shift.dtype))
 
 
-def slot_cache(bank, slot_ids) -> SlotCacheHandle:
-    return SlotCacheHandle(bank, slot_ids)
+def slot_cache(bank, slot_ids, shift_in_bank: bool = False) -> SlotCacheHandle:
+    """fla Cache over the arena rows of ``slot_ids``; see the module docstring
+    for ``shift_in_bank`` (single-token decode with install(fuse_time_mix=True)
+    only: fla's own token shift cannot read a SlotShift and raises)."""
+    return SlotCacheHandle(bank, slot_ids, shift_in_bank)

@@ -22,6 +22,8 @@ nothing here computes on the CPU.
 
 from __future__ import annotations
 
+import ctypes
+
 from typing import Sequence
 
 import torch
@@ -518,6 +520,41 @@ def slot_gather_outer_major(family: torch.Tensor, slot_dim: int, ids,
                   _ptr(out), n * row, row, _ptr(status_word(family.device)),
                   _stream(family.device))
     return out
+
+
+def wkv7_shift_mix_slots(x: torch.Tensor, mixes, shift_rows: torch.Tensor, slot_ids,
+                         out: torch.Tensor | None = None):
+    """Token shift + lerp of RWKV-7 single-token decode with the token-shift
+    state in the arena: delta = shift_rows[ids] - x (rounded to x's dtype),
+    returns (x + delta * m for m in mixes) as [B, 1, D] views and sets
+    shift_rows[ids] = x in place. shift_rows is a contiguous [S+1, D] view
+    (bank.shift[layer, family]); mixes are up to six [D]-sized parameters."""
+    _require_cuda(x, shift_rows)
+    B, D = x.shape[0], x.shape[-1]
+    if x.numel() != B * D:
+        raise ValueError("x must hold one token per row: [B, 1, D] or [B, D]")
+    if shift_rows.dim() != 2 or shift_rows.shape[1] != D or not shift_rows.is_contiguous():
+        raise ValueError("shift_rows must be a contiguous [num_slots, D] view")
+    if shift_rows.dtype != x.dtype:
+        raise ValueError("shift_rows and x must share a dtype")
+    if not 0 <= len(mixes) <= 6:
+        raise ValueError("at most six mixes")
+    x_ = x.contiguous()
+    ms = [m if (m.dtype == x.dtype and m.is_contiguous()) else m.to(x.dtype).contiguous()
+          for m in mixes]
+    if any(m.numel() != D for m in ms):
+        raise ValueError("each mix must have D elements")
+    ids = slot_ids_tensor(slot_ids, shift_rows.shape[0], x.device)
+    if ids.numel() != B:
+        raise ValueError(f"{ids.numel()} slot ids for a batch of {B}")
+    o = torch.empty(len(ms), B, 1, D, dtype=x.dtype, device=x.device) if out is None else out
+    arr = (ctypes.c_void_p * max(len(ms), 1))(*[m.data_ptr() for m in ms])
+    with torch.cuda.device(x.device):
+        _lib.call("wkvm_wkv7_shift_mix_slots", _ptr(x_), _ptr(o), _ptr(shift_rows),
+                  shift_rows.stride(0) * shift_rows.element_size(), shift_rows.shape[0],
+                  _ptr(ids), arr, len(ms), B, D, _DTYPES[x.dtype],
+                  _ptr(status_word(x.device)), _stream(x.device))
+    return tuple(o[i] for i in range(len(ms)))
 
 
 def wkv7_timemix_decode_slots(r, w_raw, k, v, v_first, v_raw, a_raw, g, k_k, k_a, r_k, gn_w,
