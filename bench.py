@@ -454,6 +454,163 @@ def run_gdn(args, world, rank, local):
     }
 
 
+def run_cfg4(args, world, rank, local):
+    """RWKV-7 7.2B-shape decode (L=32, D=4096, H=64, N=64)
+    over 512 active slots per GPU, with 5 % of the slots forked or
+    snapshotted every step and 1 % live-migrated to the next GPU.
+
+    One step on every rank:
+      decode   32 wkv7_decode_slots launches over the 512 active slots;
+      fork     13 parents copied into 13 new slots (slot_copy, all families);
+               13 other requests finish and free their slots (512 stay active);
+      snapshot 13 slots packed on the device (slot_snapshot kernel), then
+               copied to pinned host memory on a copy stream that overlaps the
+               next step (wkvm's hibernate / StateStore.save tier);
+      migrate  (N > 1) 5 slots packed and sent to rank+1 while 5 arrive from
+               rank-1 into newly allocated slots: one NCCL send/recv pair per
+               step over NVLink, the only collective traffic.
+    The migration skips shard.send_slots' host acknowledgement (a bench has
+    no peer failures to survive); the packed buffers are stream-ordered."""
+    import random
+    import torch.distributed as dist
+    from wkvm_b200 import ops, shard, synth
+    from wkvm_b200.state import RWKV7StateBank, RWKV7StateLayout
+
+    L4, H4, ACT, SLOTS = 32, 64, 512, 600
+    N_FORK, N_SNAP, N_MIG = 13, 13, (5 if world > 1 else 0)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    layout = RWKV7StateLayout(n_layer=L4, hidden_size=H4 * N, num_heads=H4, head_dim=N,
+                              head_v_dim=N, dtype=torch.bfloat16)
+    bank = RWKV7StateBank(layout, SLOTS, device=dev)
+    bank.wkv.normal_(0.0, 0.1, generator=torch.Generator(device=dev).manual_seed(99 + rank))
+    arena = shard.ShardArena(SLOTS)
+    active = arena.allocate(ACT)
+    inputs = []
+    for layer in range(L4):
+        x = synth.rwkv7_inputs(ACT, 1, H4, N, seed=rank * 1000 + layer, device=dev, state=False)
+        inputs.append([x[n] for n in ("r", "w", "k", "v", "kk", "a")])
+    outs = [torch.empty(ACT, 1, H4, N, dtype=torch.bfloat16, device=dev) for _ in range(L4)]
+    pack, unpack, empty = shard.bank_packer(bank)
+    per_slot = layout.wkv_bytes_per_slot() + layout.shift_bytes_per_slot()
+    pinned = [torch.empty(N_SNAP * per_slot, dtype=torch.uint8).pin_memory() for _ in range(2)]
+    snap_done = [None, None]
+    copy = torch.cuda.Stream(dev)
+    comp = torch.cuda.current_stream(dev)
+    ids_host = [torch.empty(ACT, dtype=torch.int32).pin_memory() for _ in range(2)]
+    ids_sent = [None, None]
+    ids_dev = torch.empty(ACT, dtype=torch.int32, device=dev)
+    rng = random.Random(1234 + rank)
+    ops.status_word(dev)
+    ops.set_decode_overlap(not args.no_overlap)
+    dec_ev = []
+
+    def step(i, timed):
+        nonlocal active
+        h = ids_host[i & 1]
+        if ids_sent[i & 1] is not None:
+            ids_sent[i & 1].synchronize()  # its previous upload has been read
+        h.copy_(torch.tensor(active, dtype=torch.int32))
+        ids_dev.copy_(h, non_blocking=True)
+        ids_sent[i & 1] = torch.cuda.Event()
+        ids_sent[i & 1].record(comp)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(comp)
+        for layer in range(L4):
+            ops.wkv7_decode_slots(*inputs[layer], bank.wkv, layer, ids_dev, out=outs[layer])
+        e1.record(comp)
+        if timed:
+            dec_ev.append((e0, e1))
+        # fork 13 parents into new slots; 13 other requests finish
+        parents = rng.sample(active, N_FORK)
+        children = arena.allocate(N_FORK)
+        ops.slot_copy(bank.wkv, 1, parents, children)
+        ops.slot_copy(bank.shift, 2, parents, children)
+        done = rng.sample([a for a in active if a not in set(parents)], N_FORK)
+        arena.free(done)
+        gone = set(done)
+        active = [a for a in active if a not in gone] + children
+        # snapshot 13 slots: device pack, then device -> pinned host on the copy stream
+        snap = rng.sample(active, N_SNAP)
+        buf = pack(snap)
+        b = i & 1
+        if snap_done[b] is not None:
+            snap_done[b].synchronize()  # that pinned buffer's previous copy landed
+        copy.wait_stream(comp)
+        with torch.cuda.stream(copy):
+            pinned[b].copy_(buf, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(copy)
+        buf.record_stream(copy)
+        snap_done[b] = ev
+        # live migration of 5 slots to the next rank, 5 in from the previous
+        if N_MIG:
+            out_ids = rng.sample(active, N_MIG)
+            sendbuf = pack(out_ids)
+            recvbuf = empty(N_MIG)
+            reqs = dist.batch_isend_irecv([
+                dist.P2POp(dist.isend, sendbuf, (rank + 1) % world),
+                dist.P2POp(dist.irecv, recvbuf, (rank - 1) % world)])
+            for r in reqs:
+                r.wait()
+            in_ids = arena.allocate(N_MIG)
+            unpack(in_ids, recvbuf)
+            arena.free(out_ids)
+            gone = set(out_ids)
+            active = [a for a in active if a not in gone] + in_ids
+
+    for i in range(args.warmup):
+        step(i, False)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index if dev.index is not None else 0) as clk:
+        start.record(comp)
+        for i in range(args.steps):
+            step(args.warmup + i, True)
+        comp.wait_stream(copy)
+        stop.record(comp)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world, dev)
+    dec_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in dec_ev) / args.steps, world, dev)
+    ops.check_device_status(dev)
+    if rank != 0:
+        return None
+    step_ms = ms / args.steps
+    dec_bytes = ACT * L4 * H4 * BYTES_PER_HEAD
+    peak, peak_kind = peaks()
+    achieved = dec_bytes / (dec_ms * 1e-3) / 1e9
+    return {
+        "metric": "RWKV-7 7.2B-shape slot decode tokens/s with fork/snapshot/migration "
+                  "(BASELINE config 4)",
+        "value": round(world * ACT * args.steps / (ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 in/out, fp32 state",
+        "data": "synthetic (seeded, reference op-level distributions)",
+        "config": {"workload": f"L={L4} D=4096 H={H4} N=64, {ACT} active of {SLOTS} arena slots "
+                               f"per GPU; per step {N_FORK} forks + {N_FORK} finished, "
+                               f"{N_SNAP} snapshots to pinned host, {N_MIG} slots migrated to "
+                               "the next GPU (NCCL send/recv)",
+                   "global_batch": ACT * world,
+                   "parallelism": f"slot-sharded x{world}; migration is the only exchange",
+                   "l2": "no flush: 35 GB of state traffic per step > 126 MB L2"},
+        "decode_ms_per_step": round(dec_ms, 4),
+        "bytes_per_step": {"decode_state": dec_bytes,
+                           "fork_copy": 2 * N_FORK * per_slot,
+                           "snapshot_d2h": N_SNAP * per_slot,
+                           "migration_nvlink_out": N_MIG * per_slot},
+        "roofline": {"bound": "hbm",
+                     "kernel": "wkv7_recurrent_kernel<64,16,bf16,mul> (wkv7_decode_slots)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
+                     "bytes_per_launch": dec_bytes // L4, "traffic": None},
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps * (L4 + 2 + 4 + (4 if N_MIG else 0)),
+    }
+
+
 def run_model_decode(args, world, rank, local):
     """BASELINE config 1 as a whole decode step: fla's RWKV-7 model (the model
     wkvm serves) at the 1.5B shape (L=24, D=2048, H=32, vocab 65536, random
@@ -693,7 +850,8 @@ def main():
     ap.add_argument("--layers", type=int, default=24,
                     help="layers per decode step (24 = the benchmark; fewer for profiling)")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "gdn-decode", "gdn-prefill", "model-decode"])
+                    choices=["decode", "prefill", "gdn-decode", "gdn-prefill", "model-decode",
+                             "cfg4"])
     ap.add_argument("--prefill-batch", type=int, default=16)
     ap.add_argument("--gdn-batch", type=int, default=4,
                     help="sequences of the gdn-prefill workload (config 3: 4)")
@@ -714,6 +872,8 @@ def main():
             line = run_model_decode(args, world, rank, local)
         elif args.workload.startswith("gdn"):
             line = run_gdn(args, world, rank, local)
+        elif args.workload == "cfg4":
+            line = run_cfg4(args, world, rank, local)
         else:
             line = run_ours(args, world, rank, local)
         if world > 1:
