@@ -611,6 +611,95 @@ def run_cfg4(args, world, rank, local):
     }
 
 
+def run_hibernate(args, world, rank, local):
+    """Snapshot tier (SURVEY next-row 3): hibernate 64 sessions of the RWKV-7
+    1.5B state shape (12.19 MiB each) from the arena to pinned host memory
+    and wake them back, batched (store_io: one kernel per family per batch)
+    versus the reference's per-session flow (wkvm/store.py:127-133: strided
+    view .copy_ into pinned memory, then a device synchronise per session)."""
+    from wkvm_b200 import ops, store_io, synth
+    from wkvm_b200.state import RWKV7StateBank, RWKV7StateLayout
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    NS = 64
+    layout = RWKV7StateLayout(n_layer=L, hidden_size=H * N, num_heads=H, head_dim=N,
+                              head_v_dim=N, dtype=torch.bfloat16)
+    bank = RWKV7StateBank(layout, NUM_SLOTS, device=dev)
+    bank.wkv.normal_(0.0, 0.1, generator=torch.Generator(device=dev).manual_seed(3))
+    sess = synth.slot_ids(NS, NUM_SLOTS + 1, seed=rank).tolist()
+    back = [s for s in range(1, NUM_SLOTS + 1) if s not in set(sess)][:NS]
+    per = layout.wkv_bytes_per_slot() + layout.shift_bytes_per_slot()
+    ops.status_word(dev)
+
+    pool = store_io.pinned_buffers(bank, NS)
+
+    def ours():  # steady state: a serving loop keeps its pinned buffers
+        return store_io.hibernate(bank, sess, pool).wait()
+
+    def ours_alloc():
+        return store_io.hibernate(bank, sess).wait()
+
+    def ref_save():
+        out = []
+        for s in sess:
+            w = torch.empty(bank.wkv[:, s].shape, dtype=torch.float32, pin_memory=True)
+            sh = torch.empty(bank.shift[:, :, s].shape, dtype=bank.shift.dtype, pin_memory=True)
+            w.copy_(bank.wkv[:, s], non_blocking=True)
+            sh.copy_(bank.shift[:, :, s], non_blocking=True)
+            torch.cuda.synchronize(dev)
+            out.append((w, sh))
+        return out
+
+    def wall(fn, reps):
+        fn()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            r = fn()
+        torch.cuda.synchronize(dev)
+        return (time.perf_counter() - t0) / reps, r
+
+    reps = max(1, args.steps)
+    t_ours, batch = wall(ours, reps)
+    t_alloc, _ = wall(ours_alloc, reps)
+    t_ref, ref_tensors = wall(ref_save, reps)
+
+    def ours_wake():
+        store_io.wake(bank, back, batch)
+
+    def ref_wake():
+        for s, (w, sh) in zip(back, ref_tensors):
+            bank.wkv[:, s].copy_(w, non_blocking=True)
+            bank.shift[:, :, s].copy_(sh, non_blocking=True)
+            torch.cuda.synchronize(dev)
+
+    t_wake, _ = wall(ours_wake, reps)
+    t_rwake, _ = wall(ref_wake, reps)
+    ok = bool(torch.equal(bank.wkv[:, back], bank.wkv[:, sess]))
+    if rank != 0:
+        return None
+    gb = NS * per / 1e9
+    return {
+        "metric": "slot hibernate (device -> pinned host) GB/s, 64 sessions of the 1.5B state",
+        "value": round(gb / t_ours, 2), "unit": "GB/s", "n_gpus": world, "steps": reps,
+        "warmup": 1, "ms_per_step": round(t_ours * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 wkv + bf16 shift (bit copies)",
+        "data": "synthetic states",
+        "config": {"workload": f"{NS} sessions x {per / 2**20:.2f} MiB, L={L} H={H} N={N}, "
+                               "host wall clock per batch incl. the final synchronise; "
+                               "reused pinned buffers"},
+        "with_new_pinned_buffers_gbs": round(gb / t_alloc, 2),
+        "wake": {"value": round(gb / t_wake, 2), "unit": "GB/s", "ms": round(t_wake * 1e3, 3),
+                 "bit_exact": ok},
+        "same_box_reference": {"hibernate_gbs": round(gb / t_ref, 2),
+                               "wake_gbs": round(gb / t_rwake, 2),
+                               "path": "per-session strided copy_ + synchronize "
+                                       "(wkvm StateStore.save / load)"},
+        "gpu_launches": 2 * reps,
+    }
+
+
 def run_model_decode(args, world, rank, local):
     """BASELINE config 1 as a whole decode step: fla's RWKV-7 model (the model
     wkvm serves) at the 1.5B shape (L=24, D=2048, H=32, vocab 65536, random
@@ -851,7 +940,7 @@ def main():
                     help="layers per decode step (24 = the benchmark; fewer for profiling)")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "gdn-decode", "gdn-prefill", "model-decode",
-                             "cfg4"])
+                             "cfg4", "hibernate"])
     ap.add_argument("--prefill-batch", type=int, default=16)
     ap.add_argument("--gdn-batch", type=int, default=4,
                     help="sequences of the gdn-prefill workload (config 3: 4)")
@@ -874,6 +963,8 @@ def main():
             line = run_gdn(args, world, rank, local)
         elif args.workload == "cfg4":
             line = run_cfg4(args, world, rank, local)
+        elif args.workload == "hibernate":
+            line = run_hibernate(args, world, rank, local)
         else:
             line = run_ours(args, world, rank, local)
         if world > 1:
