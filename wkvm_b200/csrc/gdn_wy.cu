@@ -596,24 +596,41 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
   for (int i = 0; i < cnt; ++i) {
     const int b = i & 1;
     const uint32_t da = b ? T_DA1 : T_DA0;
-    if (!wait_all(&mb_a[b], ph_a[b])) { failed = true; break; }
-    pend_a[b] = 0;
-    if (tid == 0) {  // MMA A: S^T x [W; Q~]^T
-      const uint32_t a0 = tc::smem_u32(sm + (b ? SS_A1 : SS_A0));
-      const uint32_t id = tc::idesc_tf32(128, 128);
-      for (int kk = 0; kk < KD / 8; ++kk)
-        tc::mma_tf32_ta(tm + da, tm + T_S + kk * 8, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO128),
-                        id, kk > 0);
-      tc::mma_commit(&mb_m);
+    // only the MMA issuer reads [W; Q~] (through the tensor core): thread 0
+    // alone waits for that copy
+    bool ok = true;
+    if (tid == 0) {
+      ok = tc::mbar_wait(&mb_a[b], ph_a[b]);
+      if (ok) {  // MMA A: S^T x [W; Q~]^T
+        const uint32_t a0 = tc::smem_u32(sm + (b ? SS_A1 : SS_A0));
+        const uint32_t id = tc::idesc_tf32(128, 128);
+        for (int kk = 0; kk < KD / 8; ++kk)
+          tc::mma_tf32_ta(tm + da, tm + T_S + kk * 8, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO128),
+                          id, kk > 0);
+        tc::mma_commit(&mb_m);
+      }
     }
     mma_inflight = true;
     if (i > 0) output(i - 1, b ? T_DA0 : T_DA1);  // overlaps MMA A
-    if (!wait_all(&mb_m, ph_m)) { failed = true; break; }
+    // warp 0 waits for MMA A and for the U / K~ / A_qk copy; one barrier
+    if (warp == 0) {
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      ok = ok && tc::mbar_wait(&mb_m, ph_m) && tc::mbar_wait(&mb_b, ph_b);
+    }
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+      failed = true;
+      break;
+    }
+    tc::fence_after_sync();
+    ph_a[b] ^= 1u;
+    pend_a[b] = 0;
+    ph_m ^= 1u;
     mma_inflight = false;
+    ph_b ^= 1u;
+    pend_b = 0;
     if (tid == 0 && i + 2 < cnt) issue_a(i + 2);  // MMA A has read this buffer
     if (i + 2 < cnt) pend_a[b] = 1;
-    if (!wait_all(&mb_b, ph_b)) { failed = true; break; }
-    pend_b = 0;
     {  // u^T = U^T - (W S)^T ; S^T *= e^(G_C)
       const float* ucol = reinterpret_cast<const float*>(sm + SS_B + (R_U - R_KT)) + v;
       {
