@@ -58,7 +58,8 @@ constexpr uint32_t S_TT = S_AAB + CH * RS * 4;                  // (I - A_ab)^-1
 constexpr uint32_t S_RB = S_TT + CH * RS * 4;                   // [k~; b~] -> [W^T; U~^T]
 constexpr uint32_t S_VT = S_RB + 2 * 8 * SBO;                   // V^T
 constexpr uint32_t S_ST = S_VT + 8 * SBO;                       // S^T (the running state)
-constexpr uint32_t SMEM_USED = S_ST + 8 * SBO_S;
+constexpr uint32_t S_TR = S_ST + 8 * SBO_S;                     // scratch of the inverse
+constexpr uint32_t SMEM_USED = S_TR + CH * RS * 4;
 constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;               // + alignment slack
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
@@ -154,6 +155,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
   __shared__ float s_gc[HD];    // e^{G_C}
   __shared__ float s_ref[HD];   // G at the chunk midpoint
   __shared__ float s_eref[HD];  // e^{G at the midpoint}
+  __shared__ float s_seg[NTHREADS / HD][HD];  // per-segment totals of the w scan
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3;
@@ -257,34 +259,40 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     cp_async_wait_all();
     __syncthreads();
 
-    // ---- E1: threads 0..127 scan half a column of w each; 128..255 write V^T
-    if (tid < 128) {
-      const int k = tid & 63, t0 = (tid >> 6) * 32;
+    // ---- E1: inclusive scan of w down each column by all threads: thread
+    //      (column k = tid & 63, segment tid >> 6) scans 8 tokens, then adds
+    //      the totals of the segments above; V^T is written meanwhile.
+    {
+      const int k = tid & 63, seg = tid >> 6, t0 = seg * 8;
       float acc = 0.f;
-#pragma unroll 8
-      for (int t = t0; t < t0 + 32; ++t) {
+#pragma unroll
+      for (int t = t0; t < t0 + 8; ++t) {
         acc += stg<Tin>(sm, IN_W, t, k);
         Grow[t * RS + k] = acc;
       }
-    } else if (tid < 256) {
-      const int v = tid & 63, t0 = ((tid - 128) >> 6) * 32;
+      s_seg[seg][k] = acc;
 #pragma unroll
-      for (int t = t0; t < t0 + 32; t += 4) {
-        kst4(sm + S_VT, v, t,
-             make_float4(stg<Tin>(sm, IN_V, t, v), stg<Tin>(sm, IN_V, t + 1, v),
-                         stg<Tin>(sm, IN_V, t + 2, v), stg<Tin>(sm, IN_V, t + 3, v)));
+      for (int t = t0; t < t0 + 8; t += 4)
+        kst4(sm + S_VT, k, t,
+             make_float4(stg<Tin>(sm, IN_V, t, k), stg<Tin>(sm, IN_V, t + 1, k),
+                         stg<Tin>(sm, IN_V, t + 2, k), stg<Tin>(sm, IN_V, t + 3, k)));
+      __syncthreads();
+      float off = 0.f;
+      for (int j = 0; j < seg; ++j) off += s_seg[j][k];
+      if (seg > 0) {
+#pragma unroll
+        for (int t = t0; t < t0 + 8; ++t) Grow[t * RS + k] += off;
       }
     }
     __syncthreads();
     if (tid < 128) {
       const int k = tid & 63;
-      const float mid = Grow[31 * RS + k];
       if (tid < 64) {
+        const float mid = Grow[31 * RS + k];
         s_ref[k] = mid;
         s_eref[k] = __expf(mid);
       } else {
-#pragma unroll 8
-        for (int t = 32; t < 64; ++t) Grow[t * RS + k] += mid;
+        const float mid = Grow[31 * RS + k];
         const float gc = Grow[63 * RS + k];
         s_gc[k] = __expf(gc);
         // exp(+-(G - G_mid)) must stay finite in fp32 (e^88); RWKV-7's
@@ -399,44 +407,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     }
     if (!wait_mma()) { failed = true; break; }
 
-    // ---- column phase (thread = column k, tokens of its half):
-    //      lo: Kh^T, Bh^T -> TMEM lanes k of D1's halves (A_ak, A_ab spent);
-    //      hi: (a e^Gx)^T -> T_A1 lanes 64+k, under (A_ak V)^T in lanes 0..63.
-    {
-      const int k = r64;
-      float x[CW], y[CW];
+    // ---- threads 0..255: T = (I - A_ab)^-1 as a K-major tile (row t', K = t);
+    //      threads 256..511 meanwhile, the column phase (thread = column k,
+    //      32 tokens): lo lanes Kh^T, Bh^T -> TMEM lanes k of D1's halves
+    //      (A_ak, A_ab spent); hi lanes (a e^Gx)^T -> T_A1 lanes 64+k, under
+    //      (A_ak V)^T in lanes 0..63.
+    if (tid < 256) {
+      chunkc::tri_inverse64(Aab, reinterpret_cast<float*>(sm + S_TR), sm + S_TT, tid, 256);
+    } else {
+      const int k = r64, cc0 = ((warp >> 2) - 2) * 32;
+      float x[32], y[32];
       if (lo) {
         const float gc = Grow[63 * RS + k];
 #pragma unroll
-        for (int i = 0; i < CW; ++i) {
-          const int t = c0 + i;
+        for (int i = 0; i < 32; ++i) {
+          const int t = cc0 + i;
           const float e = __expf(gc - Grow[t * RS + k]);
           x[i] = stg<Tin>(sm, IN_K, t, k) * e;
           y[i] = in_b<Tin, MUL>(sm, t, k) * e;
         }
-        tc::tmem_st(tq + T_D1 + c0, x);
-        tc::tmem_st(tq + T_D1 + 64 + c0, y);
+        tc::tmem_st32(tq + T_D1 + cc0, x);
+        tc::tmem_st32(tq + T_D1 + 64 + cc0, y);
       } else {
 #pragma unroll
-        for (int i = 0; i < CW; ++i) {
-          const int t = c0 + i;
+        for (int i = 0; i < 32; ++i) {
+          const int t = cc0 + i;
           const float a = stg<Tin>(sm, IN_5, t, k);
           x[i] = (MUL ? -a : a) * __expf(Grow[t * RS + k] - stg<Tin>(sm, IN_W, t, k));
         }
-        tc::tmem_st(tq + T_A1 + c0, x);
+        tc::tmem_st32(tq + T_A1 + cc0, x);
       }
       tc::tmem_st_wait();
     }
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
+    sync_tc();
     // The staged inputs and G are spent: stage the next chunk now so its
     // copies overlap the rest of this one.
     if (c + 1 < nchunks) stage(c + 1);
-
-    // ---- T = (I - A_ab)^-1 as a K-major tile (row t', K = t); G is spent
-    chunkc::tri_inverse64(Aab, Grow, sm + S_TT, tid);  // threads >= 256 only synchronise
-    sync_tc();
 
     // ---- MMA S: [(A_ak V)^T; (a e^Gx)^T] x T^T -> T_D3 = [U~^T; W^T]
     if (tid == 0) {

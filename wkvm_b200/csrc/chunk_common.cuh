@@ -29,12 +29,19 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // RS), blocked 16 -> 32 -> 64: the four diagonal 16-blocks by forward
 // substitution, then T_ij = T_ii A_ij T_jj for the off-diagonal blocks.
 // Written as a K-major tf32 operand tile (row t', K = t; LBO 128, SBO 2048),
-// zero above the diagonal. Trow is row-major scratch (stride RS). Must be
-// called by every thread of the CTA (256 or more); threads 256 and up only
-// take part in the barriers. Ends with the tile write, without a barrier
+// zero above the diagonal. Trow is row-major scratch (stride RS). With
+// group == 0 every thread of the CTA (256 or more) calls it and threads 256
+// and up only take part in the barriers; with group == 256 only threads
+// 0..255 call it and synchronise on named barrier 1, so the other threads of
+// the CTA can work meanwhile. Ends with the tile write, without a barrier
 // (the caller fences and synchronises before the tensor core reads it).
+__device__ __forceinline__ void group_sync(int group) {
+  if (group == 0) __syncthreads();
+  else asm volatile("bar.sync 1, %0;" :: "r"(group) : "memory");
+}
+
 __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, float* Trow,
-                                              uint8_t* tt_tile, int tid) {
+                                              uint8_t* tt_tile, int tid, int group = 0) {
   float* Tr = Trow;
   const bool act = tid < 256;
   if (tid < 64) {  // diagonal 16 x 16 blocks, one column per thread
@@ -49,7 +56,7 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
       Tr[(b0 + i) * RS + col] = y[i];
     }
   }
-  __syncthreads();
+  group_sync(group);
   // blocks (1,0) and (3,2) of 16: X = A T_jj, then T_ij = T_ii X.
   // Thread: row r = (tid >> 4) & 15, column cc = tid & 15 of both blocks.
   const int r = (tid >> 4) & 15, cc = tid & 15;
@@ -67,7 +74,7 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
 #pragma unroll
     for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[q];
   }
-  __syncthreads();
+  group_sync(group);
   if (act) {
     float yv[2] = {0.f, 0.f};
 #pragma unroll
@@ -82,12 +89,12 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
     xv[0] = yv[0];
     xv[1] = yv[1];
   }
-  __syncthreads();
+  group_sync(group);
   if (act) {
 #pragma unroll
     for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[q];
   }
-  __syncthreads();
+  group_sync(group);
   // block (1,0) of 32: X = A T_00, then T_10 = T_11 X. Thread: column
   // C = tid & 31, rows 32 + (tid >> 5) + 8 q.
   const int C = tid & 31, r0 = (tid >> 5) & 7;
@@ -103,7 +110,7 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
 #pragma unroll
     for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = xv[q];
   }
-  __syncthreads();
+  group_sync(group);
   if (act) {
     float yv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -118,12 +125,12 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
 #pragma unroll
     for (int q = 0; q < 4; ++q) xv[q] = yv[q];
   }
-  __syncthreads();
+  group_sync(group);
   if (act) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = xv[q];
   }
-  __syncthreads();
+  group_sync(group);
   if (act) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {  // K-major tile, zero above the diagonal;
