@@ -405,16 +405,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
                      tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
       tc::mma_commit(&mbar);
     }
-    if (!wait_mma()) { failed = true; break; }
 
-    // ---- threads 0..255: T = (I - A_ab)^-1 as a K-major tile (row t', K = t);
-    //      threads 256..511 meanwhile, the column phase (thread = column k,
-    //      32 tokens): lo lanes Kh^T, Bh^T -> TMEM lanes k of D1's halves
-    //      (A_ak, A_ab spent); hi lanes (a e^Gx)^T -> T_A1 lanes 64+k, under
-    //      (A_ak V)^T in lanes 0..63.
+    // ---- threads 0..255: T = (I - A_ab)^-1 as a K-major tile (row t', K = t),
+    //      while MMA 2 runs; threads 256..511 wait for MMA 2, then the column
+    //      phase (thread = column k, 32 tokens): lo lanes Kh^T, Bh^T -> TMEM
+    //      lanes k of D1's halves (A_ak, A_ab spent); hi lanes (a e^Gx)^T ->
+    //      T_A1 lanes 64+k, under (A_ak V)^T in lanes 0..63.
+    bool ok2 = true;
     if (tid < 256) {
       chunkc::tri_inverse64(Aab, reinterpret_cast<float*>(sm + S_TR), sm + S_TT, tid, 256);
+    } else if (!(ok2 = tc::mbar_wait(&mbar, phase))) {
+      // reported below
     } else {
+      tc::fence_after_sync();
       const int k = r64, cc0 = ((warp >> 2) - 2) * 32;
       float x[32], y[32];
       if (lo) {
@@ -439,7 +442,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
       }
       tc::tmem_st_wait();
     }
-    sync_tc();
+    phase ^= 1u;
+    tc::fence_smem_to_async();
+    tc::fence_before_sync();
+    if (__syncthreads_or(!ok2)) {
+      if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+      failed = true;
+      break;
+    }
+    tc::fence_after_sync();
     // The staged inputs and G are spent: stage the next chunk now so its
     // copies overlap the rest of this one.
     if (c + 1 < nchunks) stage(c + 1);
