@@ -533,6 +533,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     tc::tmem_st32(tq + T_S + kb, x);
   }
   tc::tmem_st_wait();
+  // every thread's share of S^T is in TMEM before thread 0 issues MMA A
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
 
   uint32_t ph_a[2] = {0, 0}, ph_b = 0, ph_m = 0;
   int pend_a[2] = {0, 0}, pend_b = 0;  // copies issued and not yet waited for
