@@ -85,28 +85,6 @@ __device__ __forceinline__ void sync_tc() {
   tc::fence_after_sync();
 }
 
-__device__ __forceinline__ float sel4(float a0, float a1, float a2, float a3, int i) {
-  return i == 0 ? a0 : i == 1 ? a1 : i == 2 ? a2 : a3;
-}
-
-// 4 x 4 transpose inside each quad of lanes: on entry lane q of the quad holds
-// a[c] = M[c][q]; on exit it holds b[r] = M[q][r].
-__device__ __forceinline__ float4 quad_transpose(const float (&a)[4], int lane) {
-  const int q = lane & 3;
-  float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-#pragma unroll
-  for (int d = 0; d < 4; ++d) {
-    const int r = (q - d) & 3;  // source lane within the quad
-    const float send = sel4(a[0], a[1], a[2], a[3], (q + d) & 3);
-    const float got = d == 0 ? send : __shfl_sync(0xffffffffu, send, (lane & ~3) | r);
-    if (r == 0) b0 = got;
-    if (r == 1) b1 = got;
-    if (r == 2) b2 = got;
-    if (r == 3) b3 = got;
-  }
-  return make_float4(b0, b1, b2, b3);
-}
-
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) &
                                     ~static_cast<uintptr_t>(1023));
@@ -131,6 +109,8 @@ constexpr uint32_t WS_TR = WS_AAB + CH * RS * 4;
 constexpr uint32_t WS_TT = WS_AAB;                    // written after -A is spent
 static_assert(WS_TR + CH * RS * 4 <= STAGE, "inverse scratch outside the stage");
 constexpr uint32_t WY_SMEM = 2 * STAGE + 1024;
+constexpr int W_ROW = KD + 4;  // row stride (floats) of W staged row-major in a spent stage
+static_assert(CH * W_ROW * 4 <= STAGE, "W staging outside the stage");
 // TMEM: MMA 1 accumulator, later U^T | (beta v)^T | (beta e^G k^)^T | W^T
 constexpr uint32_t WY_TMEM_COLS = 256;
 constexpr uint32_t T_D1 = 0, T_AV = 64, T_AK = 128, T_DW = 192;
@@ -425,16 +405,25 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
         float* ucol = reinterpret_cast<float*>(rec + R_U) + l;
 #pragma unroll
         for (int i = 0; i < 32; ++i) ucol[(t0 + i) * VD] = x[i];
-        tc::tmem_ld32(tq + T_DW + t0, x);  // W^T[k = l][t0 + i]
-        // lane l of quad m gets W[t0 + 4j + (l & 3)][4m .. 4m+3]: 16-byte stores
+        // W^T[k = l][t0 + i] -> row-major W[t][k] in the spent stage (row
+        // stride W_ROW: lanes hit distinct banks), copied out below
+        tc::tmem_ld32(tq + T_DW + t0, x);
+        float* wst = reinterpret_cast<float*>(sg);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) wst[(t0 + i) * W_ROW + l] = x[i];
+        if (tid == 0) *reinterpret_cast<float*>(rec + R_META) = __expf(GC);
+      }
+      __syncthreads();
+      {  // W -> the record's K-major [W] rows: eight lanes fill one 128-byte core
+         // matrix row group, a warp 512 contiguous bytes
+        const float* wst = reinterpret_cast<const float*>(sg);
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
-          const float a[4] = {x[4 * jj], x[4 * jj + 1], x[4 * jj + 2], x[4 * jj + 3]};
-          const float4 w4 = quad_transpose(a, lane);
-          *reinterpret_cast<float4*>(rec + R_WQ + tc::kmajor_off(t0 + 4 * jj + (l & 3), l & ~3, LBO,
-                                                                  SBO128)) = w4;
+          const int e = tid + WY_THREADS * jj;
+          const int t = (e >> 8) * 8 + (e & 7), k4 = ((e >> 3) & 31) * 4;
+          *reinterpret_cast<float4*>(rec + R_WQ + tc::kmajor_off(t, k4, LBO, SBO128)) =
+              *reinterpret_cast<const float4*>(wst + t * W_ROW + k4);
         }
-        if (tid == 0) *reinterpret_cast<float*>(rec + R_META) = __expf(GC);
       }
       // the next job overwrites this stage only after every thread is past here
       tc::fence_before_sync();
