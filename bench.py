@@ -20,6 +20,12 @@ flush is needed between steps.
 
 Multi-GPU: one process per GPU (torchrun), each GPU holds its own arena
 shard and 256 active slots; no collective on the data path (weak scaling).
+
+Other workloads (--workload): prefill (config 2, RWKV-7 chunk prefill into
+slots), gdn-decode / gdn-prefill (config 3), model-decode (config 1 as fla's
+whole RWKV-7 model step), cfg4 (config 4: 7.2B-shape decode with forks,
+host snapshots and NCCL slot migration every step) and hibernate (batched
+snapshot / wake of 64 sessions against wkvm's per-session copies).
 ``--impl reference`` times the CPU restatement of the reference recurrence
 (oracle/, fp32, all host threads) on a bounded sample of the same workload.
 """

@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
   const int nchunks = (int)((len + CH - 1) / CH);
 
   auto wait_mma = [&]() -> bool {
-    const bool ok = tc::mbar_wait(&mbar, phase);
+    const bool ok = warp != 0 || tc::mbar_wait(&mbar, phase);  // warp 0 polls
     phase ^= 1u;
     const bool any_bad = __syncthreads_or(!ok);
     tc::fence_after_sync();

@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
         }
         tc::tmem_st_wait();
       }
-      bool ok = tc::mbar_wait(&mbar, 0);
+      bool ok = warp != 0 || tc::mbar_wait(&mbar, 0);  // warp 0 polls
       if (__syncthreads_or(!ok)) {  // give the MMA one more bounded wait before TMEM goes
         if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
         tc::mbar_wait(&mbar, 0);
@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
                           id_s, kk > 0);
         tc::mma_commit(&mbar);
       }
-      ok = tc::mbar_wait(&mbar, 1);
+      ok = warp != 0 || tc::mbar_wait(&mbar, 1);
       if (__syncthreads_or(!ok)) {
         if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
         tc::mbar_wait(&mbar, 1);
