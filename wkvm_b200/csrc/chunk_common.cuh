@@ -40,6 +40,15 @@ __device__ __forceinline__ void group_sync(int group) {
   else asm volatile("bar.sync 1, %0;" :: "r"(group) : "memory");
 }
 
+__device__ __forceinline__ float4 ld4(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+
+// Rows of A and T are read as float4 (16-byte aligned: RS and every column
+// offset used are multiples of 4), columns as scalars; the diagonal 16-blocks
+// and the two upper 16-blocks the 32-merges read (rows 0..15 x cols 16..31,
+// rows 32..47 x cols 48..63) are written with their zeros, so no product
+// needs a mask.
 __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, float* Trow,
                                               uint8_t* tt_tile, int tid, int group = 0) {
   float* Tr = Trow;
@@ -49,11 +58,27 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
     float y[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
+      const float* ar = Aab + (b0 + i) * RS + b0;
+      float a[16];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        if (4 * q4 < i) {
+          const float4 t4 = ld4(ar + 4 * q4);
+          a[4 * q4] = t4.x;
+          a[4 * q4 + 1] = t4.y;
+          a[4 * q4 + 2] = t4.z;
+          a[4 * q4 + 3] = t4.w;
+        }
+      }
       float v = (i == ci) ? 1.f : 0.f;
 #pragma unroll
-      for (int i2 = 0; i2 < i; ++i2) v = fmaf(Aab[(b0 + i) * RS + b0 + i2], y[i2], v);
+      for (int i2 = 0; i2 < i; ++i2) v = fmaf(a[i2], y[i2], v);
       y[i] = (i < ci) ? 0.f : v;
       Tr[(b0 + i) * RS + col] = y[i];
+    }
+    if (b0 & 16) {  // the 16-block above this diagonal block is zero
+#pragma unroll
+      for (int i = 0; i < 16; ++i) Tr[(b0 - 16 + i) * RS + col] = 0.f;
     }
   }
   group_sync(group);
@@ -63,36 +88,45 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
   float xv[4] = {0.f, 0.f, 0.f, 0.f};
   if (act) {
 #pragma unroll
-    for (int s2 = 0; s2 < 16; ++s2) {
+    for (int q = 0; q < 2; ++q) {
+      const float* ar = Aab + (32 * q + 16 + r) * RS + 32 * q;
+      const float* tc0 = Tr + (32 * q) * RS + 32 * q + cc;
+      float x = 0.f;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const float tv = Tr[(32 * q + s2) * RS + 32 * q + cc];
-        const float av = Aab[(32 * q + 16 + r) * RS + 32 * q + s2];
-        xv[q] = fmaf(av, s2 >= cc ? tv : 0.f, xv[q]);
+      for (int s4 = 0; s4 < 16; s4 += 4) {
+        const float4 a4 = ld4(ar + s4);
+        x = fmaf(a4.x, tc0[(s4 + 0) * RS], x);
+        x = fmaf(a4.y, tc0[(s4 + 1) * RS], x);
+        x = fmaf(a4.z, tc0[(s4 + 2) * RS], x);
+        x = fmaf(a4.w, tc0[(s4 + 3) * RS], x);
       }
+      xv[q] = x;
     }
 #pragma unroll
     for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[q];
   }
   group_sync(group);
   if (act) {
-    float yv[2] = {0.f, 0.f};
 #pragma unroll
-    for (int s2 = 0; s2 < 16; ++s2) {
+    for (int q = 0; q < 2; ++q) {
+      const float* tr = Tr + (32 * q + 16 + r) * RS + 32 * q + 16;
+      const float* xc = Tr + (32 * q + 16) * RS + 32 * q + cc;
+      float y = 0.f;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const float tv = Tr[(32 * q + 16 + r) * RS + 32 * q + 16 + s2];
-        const float xx = Tr[(32 * q + 16 + s2) * RS + 32 * q + cc];
-        yv[q] = fmaf(s2 <= r ? tv : 0.f, xx, yv[q]);
+      for (int s4 = 0; s4 < 16; s4 += 4) {
+        const float4 t4 = ld4(tr + s4);
+        y = fmaf(t4.x, xc[(s4 + 0) * RS], y);
+        y = fmaf(t4.y, xc[(s4 + 1) * RS], y);
+        y = fmaf(t4.z, xc[(s4 + 2) * RS], y);
+        y = fmaf(t4.w, xc[(s4 + 3) * RS], y);
       }
+      xv[2 + q] = y;
     }
-    xv[0] = yv[0];
-    xv[1] = yv[1];
   }
   group_sync(group);
   if (act) {
 #pragma unroll
-    for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[q];
+    for (int q = 0; q < 2; ++q) Tr[(32 * q + 16 + r) * RS + 32 * q + cc] = xv[2 + q];
   }
   group_sync(group);
   // block (1,0) of 32: X = A T_00, then T_10 = T_11 X. Thread: column
@@ -102,10 +136,18 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
 #pragma unroll
     for (int q = 0; q < 4; ++q) xv[q] = 0.f;
 #pragma unroll
-    for (int s2 = 0; s2 < 32; ++s2) {
-      const float tv = s2 >= C ? Tr[s2 * RS + C] : 0.f;
+    for (int s4 = 0; s4 < 32; s4 += 4) {
+      float tv[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) xv[q] = fmaf(Aab[(32 + r0 + 8 * q) * RS + s2], tv, xv[q]);
+      for (int i = 0; i < 4; ++i) tv[i] = Tr[(s4 + i) * RS + C];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 a4 = ld4(Aab + (32 + r0 + 8 * q) * RS + s4);
+        xv[q] = fmaf(a4.x, tv[0], xv[q]);
+        xv[q] = fmaf(a4.y, tv[1], xv[q]);
+        xv[q] = fmaf(a4.z, tv[2], xv[q]);
+        xv[q] = fmaf(a4.w, tv[3], xv[q]);
+      }
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) Tr[(32 + r0 + 8 * q) * RS + C] = xv[q];
@@ -114,12 +156,17 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
   if (act) {
     float yv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int s2 = 0; s2 < 32; ++s2) {
-      const float xx = Tr[(32 + s2) * RS + C];
+    for (int s4 = 0; s4 < 32; s4 += 4) {
+      float xx[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xx[i] = Tr[(32 + s4 + i) * RS + C];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const int R = r0 + 8 * q;
-        yv[q] = fmaf(s2 <= R ? Tr[(32 + R) * RS + 32 + s2] : 0.f, xx, yv[q]);
+        const float4 t4 = ld4(Tr + (32 + r0 + 8 * q) * RS + 32 + s4);
+        yv[q] = fmaf(t4.x, xx[0], yv[q]);
+        yv[q] = fmaf(t4.y, xx[1], yv[q]);
+        yv[q] = fmaf(t4.z, xx[2], yv[q]);
+        yv[q] = fmaf(t4.w, xx[3], yv[q]);
       }
     }
 #pragma unroll
