@@ -53,33 +53,90 @@ __device__ __forceinline__ void tri_inverse64(const float* __restrict__ Aab, flo
                                               uint8_t* tt_tile, int tid, int group = 0) {
   float* Tr = Trow;
   const bool act = tid < 256;
-  if (tid < 64) {  // diagonal 16 x 16 blocks, one column per thread
-    const int col = tid, b0 = col & ~15, ci = col & 15;
-    float y[16];
+  // ---- stage 1: the four diagonal 16 x 16 blocks, one warp each (warps 0..3,
+  //      lane ln), blocked 4 -> 8 -> 16 with warp-level synchronisation; every
+  //      block above a diagonal block that a later product reads is written as
+  //      zero.
+  if (act && tid < 128) {
+    const int ln = tid & 31, blk = tid >> 5, b0 = blk * 16;
+    if (ln < 16) {  // 4 x 4 diagonal blocks: column c of sub-block sb
+      const int c = ln, sb = c >> 2, ci = c & 3, r0 = b0 + sb * 4;
+      const float4 a1 = ld4(Aab + (r0 + 1) * RS + r0), a2 = ld4(Aab + (r0 + 2) * RS + r0),
+                   a3 = ld4(Aab + (r0 + 3) * RS + r0);
+      const float y0 = ci == 0 ? 1.f : 0.f;
+      float y1 = fmaf(a1.x, y0, ci == 1 ? 1.f : 0.f);
+      y1 = ci > 1 ? 0.f : y1;
+      float y2 = fmaf(a2.y, y1, fmaf(a2.x, y0, ci == 2 ? 1.f : 0.f));
+      y2 = ci > 2 ? 0.f : y2;
+      const float y3 = fmaf(a3.z, y2, fmaf(a3.y, y1, fmaf(a3.x, y0, ci == 3 ? 1.f : 0.f)));
+      float* tc0 = Tr + r0 * RS + b0 + c;
+      tc0[0] = y0;
+      tc0[RS] = y1;
+      tc0[2 * RS] = y2;
+      tc0[3 * RS] = y3;
+      if (sb & 1) {  // the 4-block above is zero
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float* ar = Aab + (b0 + i) * RS + b0;
-      float a[16];
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        if (4 * q4 < i) {
-          const float4 t4 = ld4(ar + 4 * q4);
-          a[4 * q4] = t4.x;
-          a[4 * q4 + 1] = t4.y;
-          a[4 * q4 + 2] = t4.z;
-          a[4 * q4 + 3] = t4.w;
-        }
+        for (int i = 0; i < 4; ++i) tc0[(i - 4) * RS] = 0.f;
       }
-      float v = (i == ci) ? 1.f : 0.f;
+      if (sb >= 2) {  // and the 8-block above, rows b0 .. b0+7
 #pragma unroll
-      for (int i2 = 0; i2 < i; ++i2) v = fmaf(a[i2], y[i2], v);
-      y[i] = (i < ci) ? 0.f : v;
-      Tr[(b0 + i) * RS + col] = y[i];
-    }
-    if (b0 & 16) {  // the 16-block above this diagonal block is zero
+        for (int i = 0; i < 8; ++i) Tr[(b0 + i) * RS + b0 + c] = 0.f;
+      }
+      if (blk & 1) {  // and the 16-block above this diagonal block
 #pragma unroll
-      for (int i = 0; i < 16; ++i) Tr[(b0 - 16 + i) * RS + col] = 0.f;
+        for (int i = 0; i < 16; ++i) Tr[(b0 - 16 + i) * RS + b0 + c] = 0.f;
+      }
     }
+    __syncwarp();
+    // 4 -> 8: blocks (1,0) of each 8 x 8 diagonal block (m = 0, 1)
+    const int m = ln >> 4, r = (ln >> 2) & 3, cc = ln & 3, e0 = b0 + 8 * m;
+    {
+      const float4 a4 = ld4(Aab + (e0 + 4 + r) * RS + e0);
+      const float* tcol = Tr + e0 * RS + e0 + cc;
+      const float xq = fmaf(a4.x, tcol[0], fmaf(a4.y, tcol[RS], fmaf(a4.z, tcol[2 * RS],
+                            a4.w * tcol[3 * RS])));
+      Tr[(e0 + 4 + r) * RS + e0 + cc] = xq;
+    }
+    __syncwarp();
+    float yq;
+    {
+      const float4 t4 = ld4(Tr + (e0 + 4 + r) * RS + e0 + 4);
+      const float* xc = Tr + (e0 + 4) * RS + e0 + cc;
+      yq = fmaf(t4.x, xc[0], fmaf(t4.y, xc[RS], fmaf(t4.z, xc[2 * RS], t4.w * xc[3 * RS])));
+    }
+    __syncwarp();
+    Tr[(e0 + 4 + r) * RS + e0 + cc] = yq;
+    __syncwarp();
+    // 8 -> 16: block (1,0) of the 16 x 16 diagonal block, X = A_10 T_00, T_10 = T_11 X;
+    // lane: column c8, rows r8 and r8 + 4
+    const int c8 = ln & 7, ra = ln >> 3;
+    float x8[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r8 = ra + 4 * h;
+      const float4 a0 = ld4(Aab + (b0 + 8 + r8) * RS + b0),
+                   a1 = ld4(Aab + (b0 + 8 + r8) * RS + b0 + 4);
+      const float* tcol = Tr + b0 * RS + b0 + c8;
+      x8[h] = fmaf(a0.x, tcol[0], fmaf(a0.y, tcol[RS], fmaf(a0.z, tcol[2 * RS],
+              fmaf(a0.w, tcol[3 * RS], fmaf(a1.x, tcol[4 * RS], fmaf(a1.y, tcol[5 * RS],
+              fmaf(a1.z, tcol[6 * RS], a1.w * tcol[7 * RS])))))));
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) Tr[(b0 + 8 + ra + 4 * h) * RS + b0 + c8] = x8[h];
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r8 = ra + 4 * h;
+      const float4 t0 = ld4(Tr + (b0 + 8 + r8) * RS + b0 + 8),
+                   t1 = ld4(Tr + (b0 + 8 + r8) * RS + b0 + 12);
+      const float* xc = Tr + (b0 + 8) * RS + b0 + c8;
+      x8[h] = fmaf(t0.x, xc[0], fmaf(t0.y, xc[RS], fmaf(t0.z, xc[2 * RS],
+              fmaf(t0.w, xc[3 * RS], fmaf(t1.x, xc[4 * RS], fmaf(t1.y, xc[5 * RS],
+              fmaf(t1.z, xc[6 * RS], t1.w * xc[7 * RS])))))));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) Tr[(b0 + 8 + ra + 4 * h) * RS + b0 + c8] = x8[h];
   }
   group_sync(group);
   // blocks (1,0) and (3,2) of 16: X = A T_jj, then T_ij = T_ii X.
