@@ -37,12 +37,17 @@ __global__ void __launch_bounds__(256) shift_mix_kernel(MixArgs p) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= (int64_t)p.B * D8) return;
   const int b = (int)(e / D8), d0 = (int)(e - (int64_t)b * D8) * 8;
+  // every load that does not depend on the slot id goes out first
   const int32_t s = p.ids[b];
+  const uint4 xu = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.x) + (int64_t)b * p.D + d0);
+  uint4 mu[kMaxMix];
+#pragma unroll
+  for (int m = 0; m < kMaxMix; ++m)
+    if (m < p.n_mix) mu[m] = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.mix[m]) + d0);
   if (s < 0 || (int64_t)s >= p.num_slots) {
     if (d0 == 0) report(p.status, WKVM_ERR_SLOT_RANGE);
     return;
   }
-  const uint4 xu = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.x) + (int64_t)b * p.D + d0);
   uint4* srow = reinterpret_cast<uint4*>(p.shift + (int64_t)s * p.slot_stride + (int64_t)d0 * 2);
   const uint4 pu = *srow;
   const T* xe = reinterpret_cast<const T*>(&xu);
@@ -54,9 +59,10 @@ __global__ void __launch_bounds__(256) shift_mix_kernel(MixArgs p) {
     dv[i] = to_f32(from_f32<T>(__fsub_rn(to_f32(pe[i]), xv[i])));  // delta is stored 16-bit
   }
   *srow = xu;
-  for (int m = 0; m < p.n_mix; ++m) {
-    const uint4 mu = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.mix[m]) + d0);
-    const T* me = reinterpret_cast<const T*>(&mu);
+#pragma unroll
+  for (int m = 0; m < kMaxMix; ++m) {
+    if (m >= p.n_mix) break;
+    const T* me = reinterpret_cast<const T*>(&mu[m]);
     uint4 ou;
     T* oe = reinterpret_cast<T*>(&ou);
 #pragma unroll
