@@ -407,31 +407,35 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     }
 
     // ---- threads 0..255: T = (I - A_ab)^-1 as a K-major tile (row t', K = t),
-    //      while MMA 2 runs; threads 256..511 wait for MMA 2, then the column
-    //      phase (thread = column k, 32 tokens): lo lanes Kh^T, Bh^T -> TMEM
-    //      lanes k of D1's halves (A_ak, A_ab spent); hi lanes (a e^Gx)^T ->
-    //      T_A1 lanes 64+k, under (A_ak V)^T in lanes 0..63.
+    //      while MMA 2 runs; threads 256..511, the column phase (thread =
+    //      column k, 32 tokens): lo lanes Kh^T, Bh^T -> TMEM lanes k of D1's
+    //      halves (A_ak, A_ab spent) at once; hi lanes, once MMA 2 is done,
+    //      (a e^Gx)^T -> T_A1 lanes 64+k, under (A_ak V)^T in lanes 0..63.
     bool ok2 = true;
     if (tid < 256) {
       chunkc::tri_inverse64(Aab, reinterpret_cast<float*>(sm + S_TR), sm + S_TT, tid, 256);
-    } else if (!(ok2 = tc::mbar_wait(&mbar, phase))) {
-      // reported below
+    } else if (!lo && !(ok2 = tc::mbar_wait(&mbar, phase))) {
+      // reported below (only the hi lanes write where MMA 2 writes)
     } else {
       tc::fence_after_sync();
       const int k = r64, cc0 = ((warp >> 2) - 2) * 32;
-      float x[32], y[32];
-      if (lo) {
+      if (lo) {  // two halves of 16 tokens keep the live registers down
         const float gc = Grow[63 * RS + k];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int t = cc0 + i;
-          const float e = __expf(gc - Grow[t * RS + k]);
-          x[i] = stg<Tin>(sm, IN_K, t, k) * e;
-          y[i] = in_b<Tin, MUL>(sm, t, k) * e;
+        for (int hh = 0; hh < 32; hh += 16) {
+          float x[16], y[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int t = cc0 + hh + i;
+            const float e = __expf(gc - Grow[t * RS + k]);
+            x[i] = stg<Tin>(sm, IN_K, t, k) * e;
+            y[i] = in_b<Tin, MUL>(sm, t, k) * e;
+          }
+          tc::tmem_st16(tq + T_D1 + cc0 + hh, x);
+          tc::tmem_st16(tq + T_D1 + 64 + cc0 + hh, y);
         }
-        tc::tmem_st32(tq + T_D1 + cc0, x);
-        tc::tmem_st32(tq + T_D1 + 64 + cc0, y);
       } else {
+        float x[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int t = cc0 + i;
