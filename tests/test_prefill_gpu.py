@@ -25,7 +25,7 @@ def _ab(d):
 
 
 @pytest.mark.parametrize("T", [1, 63, 64, 200])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("h0", [True, False])
 def test_chunk_rwkv7_matches_oracle(cuda, T, dtype, h0):
     B, H, N = 2, 3, 64
@@ -149,6 +149,22 @@ def test_chunk_gdn_matches_oracle(cuda, gdn_path, T, hv_mult, l2):
     ro, rh = oracle.gdn_recurrence(*(np32(x[n]) for n in GDN), initial_state=np32(x["h0"]),
                                    use_qk_l2norm=l2)
     ops.check_device_status(cuda)
+    assert_out_close(o, ro)
+    assert rel_err(ht, rh) < REL_TOL
+
+
+def test_chunk_gdn_fp16_inputs(cuda, gdn_path):
+    # fp16 runs the Gram block on fp16 operands (kind::f16, both operands fp16)
+    B, T, H, K = 2, 200, 2, 128
+    x = synth.gdn_inputs(B, T, H, K, HV=4, seed=12, dtype=torch.float16)
+    d = _to(x, cuda)
+    o, ht = ops.chunk_gated_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"],
+                                       initial_state=d["h0"], output_final_state=True,
+                                       use_qk_l2norm_in_kernel=True)
+    ro, rh = oracle.gdn_recurrence(*(np32(x[n]) for n in GDN), initial_state=np32(x["h0"]),
+                                   use_qk_l2norm=True)
+    ops.check_device_status(cuda)
+    assert o.dtype == torch.float16
     assert_out_close(o, ro)
     assert rel_err(ht, rh) < REL_TOL
 
