@@ -706,6 +706,86 @@ def run_hibernate(args, world, rank, local):
     }
 
 
+def run_timemix(args, world, rank, local):
+    """The fused time-mix decode core alone at the BASELINE config 1 shape:
+    24 wkv7_timemix_decode_slots launches per step (layer 0 without v_first),
+    256 active of 1024 arena slots, H=32, N=64, as a CUDA graph. Bytes per
+    launch: the head states read and written (256 x 32 x 32 KiB) + the eight
+    activation rows in, one out, the per-channel parameters."""
+    from wkvm_b200 import ops, synth
+    from wkvm_b200.state import RWKV7StateBank, RWKV7StateLayout
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    D = H * N
+    layout = RWKV7StateLayout(n_layer=L, hidden_size=D, num_heads=H, head_dim=N, head_v_dim=N,
+                              dtype=torch.bfloat16)
+    bank = RWKV7StateBank(layout, NUM_SLOTS, device=dev)
+    bank.wkv.normal_(0.0, 0.1, generator=torch.Generator(device=dev).manual_seed(5 + rank))
+    ids = ops.slot_ids_tensor(synth.slot_ids(ACTIVE, NUM_SLOTS + 1, seed=rank).tolist(),
+                              NUM_SLOTS + 1, dev)
+    g = torch.Generator(device=dev).manual_seed(17 + rank)
+    mk = lambda *sh, sc=1.0: (torch.randn(*sh, device=dev, generator=g) * sc).to(torch.bfloat16)
+    acts = [[mk(ACTIVE, D) for _ in range(8)] for _ in range(L)]  # r w k v v_first v_raw a g
+    prm = [[mk(D, sc=0.5), mk(D, sc=0.5), mk(H, N, sc=0.5), mk(D, sc=0.3), mk(D, sc=0.1)]
+           for _ in range(L)]
+    outs = [torch.empty(ACTIVE, D, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+    ops.status_word(dev)
+
+    def step():
+        for layer in range(L):
+            r, w, k, v, vf, vr, a, gg = acts[layer]
+            kk_, ka, rk, gw, gb = prm[layer]
+            ops.wkv7_timemix_decode_slots(r, w, k, v, vf if layer else None, vr if layer else None,
+                                          a, gg, kk_, ka, rk, gw, gb, 64e-5, bank.wkv, layer, ids,
+                                          out=outs[layer])
+
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index if dev.index is not None else 0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record()
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world, dev)
+    ops.check_device_status(dev)
+    if rank != 0:
+        return None
+    step_ms = ms / args.steps
+    per_launch = ACTIVE * H * 2 * N * N * 4 + ACTIVE * D * 2 * 9 + D * 2 * 5
+    achieved = per_launch / (step_ms / L * 1e-3) / 1e9
+    peak, kind = peaks()
+    return {
+        "metric": "fused RWKV-7 time-mix decode core tokens/s (config 1 shape)",
+        "value": round(world * ACTIVE * args.steps / (ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 in/out, fp32 state and arithmetic",
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"L={L} H={H} N={N}, {ACTIVE} active of {NUM_SLOTS} slots, "
+                               "CUDA graph of the 24 launches"},
+        "roofline": {"bound": "hbm", "kernel": "wkv7_timemix_decode_kernel<bf16>",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{kind} hbm_gbs",
+                     "bytes_per_launch": per_launch, "traffic": None},
+        "clocks": clk.summary(), "gpu_launches": L * args.steps,
+    }
+
+
 def run_model_decode(args, world, rank, local):
     """BASELINE config 1 as a whole decode step: fla's RWKV-7 model (the model
     wkvm serves) at the 1.5B shape (L=24, D=2048, H=32, vocab 65536, random
@@ -946,7 +1026,7 @@ def main():
                     help="layers per decode step (24 = the benchmark; fewer for profiling)")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "gdn-decode", "gdn-prefill", "model-decode",
-                             "cfg4", "hibernate"])
+                             "cfg4", "hibernate", "timemix"])
     ap.add_argument("--prefill-batch", type=int, default=16)
     ap.add_argument("--gdn-batch", type=int, default=4,
                     help="sequences of the gdn-prefill workload (config 3: 4)")
@@ -971,6 +1051,8 @@ def main():
             line = run_cfg4(args, world, rank, local)
         elif args.workload == "hibernate":
             line = run_hibernate(args, world, rank, local)
+        elif args.workload == "timemix":
+            line = run_timemix(args, world, rank, local)
         else:
             line = run_ours(args, world, rank, local)
         if world > 1:

@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(NT) wkv7_timemix_decode_kernel(TmArgs p) {
   __shared__ __align__(16) float s_in[6][N];  // 0 e^w, 1 -kk, 2 kk*a, 3 k', 4 r e^w, 5 v
   __shared__ __align__(16) float s_red[RG][2][N];
   __shared__ float s_dot[2][4];               // per staging warp: r.b, r.k', r.k'.r_k, |k k_k|^2
-  __shared__ float s_misc[2];
+  __shared__ __align__(16) float s_ep[3][N];  // epilogue inputs: g, gn_w, gn_b
 
   const int H = p.H;
   const int n = blockIdx.x / H, hh = blockIdx.x - (blockIdx.x / H) * H;
@@ -87,6 +87,10 @@ __global__ void __launch_bounds__(NT) wkv7_timemix_decode_kernel(TmArgs p) {
   const float kkr = kraw * to_f32(static_cast<const T*>(p.k_k)[ch]);
   const float kup = fmaf(kraw * (aa - 1.0f), to_f32(static_cast<const T*>(p.k_a)[ch]), kraw);
   const float rkk = to_f32(static_cast<const T*>(p.r_k)[ch]);
+  // the epilogue's inputs are loaded now, with the rest of the staging
+  s_ep[0][tid] = to_f32(static_cast<const T*>(p.g)[base]);
+  s_ep[1][tid] = to_f32(static_cast<const T*>(p.gn_w)[ch]);
+  s_ep[2][tid] = to_f32(static_cast<const T*>(p.gn_b)[ch]);
   // per-head sums: |k k_k|^2 first (kk needs it)
   float part_nn = wsum(kkr * kkr);
   if (lane == 0) s_dot[warp][3] = part_nn;
@@ -168,16 +172,13 @@ __global__ void __launch_bounds__(NT) wkv7_timemix_decode_kernel(TmArgs p) {
       T* op = static_cast<T*>(p.o) + ((int64_t)n * H + hh) * N + cg * 4;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int c = hh * N + cg * 4 + i;
-        const float gw = to_f32(static_cast<const T*>(p.gn_w)[c]);
-        const float gb = to_f32(static_cast<const T*>(p.gn_b)[c]);
-        const float gg = to_f32(static_cast<const T*>(p.g)[((int64_t)n * H + hh) * N + cg * 4 + i]);
+        const int c = cg * 4 + i;
+        const float gg = s_ep[0][c], gw = s_ep[1][c], gb = s_ep[2][c];
         const float on = fmaf((o4[i] - mean) * rstd, gw, gb);
         op[i] = from_f32<T>(fmaf(corr, vals[i], on) * gg);
       }
     }
   }
-  (void)s_misc;
 }
 
 }  // namespace
