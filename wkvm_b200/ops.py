@@ -24,7 +24,6 @@ from __future__ import annotations
 
 import ctypes
 
-from typing import Sequence
 
 import torch
 
