@@ -24,7 +24,6 @@ from __future__ import annotations
 
 import ctypes
 
-
 import torch
 
 from . import _lib
