@@ -63,12 +63,6 @@ __global__ void __launch_bounds__(NT) wkv7_timemix_decode_kernel(TmArgs p) {
     return;
   }
   const int64_t hoff = ((int64_t)id * H + hh) * (N * N);
-  float4 hreg[ROWS];
-  {
-    const float* src = p.bank + hoff + cg * 4;
-#pragma unroll
-    for (int j = 0; j < ROWS; ++j) hreg[j] = ld_stream_f4(src + (j * RG + rg) * N);
-  }
 
   // ---- staging: thread e = tid owns channel e of this head
   const int64_t base = ((int64_t)n * H + hh) * N + tid;
@@ -91,6 +85,14 @@ __global__ void __launch_bounds__(NT) wkv7_timemix_decode_kernel(TmArgs p) {
   s_ep[0][tid] = to_f32(static_cast<const T*>(p.g)[base]);
   s_ep[1][tid] = to_f32(static_cast<const T*>(p.gn_w)[ch]);
   s_ep[2][tid] = to_f32(static_cast<const T*>(p.gn_b)[ch]);
+  // the state loads go out after the activation loads they would otherwise
+  // delay (the gates below are the first dependent chain)
+  float4 hreg[ROWS];
+  {
+    const float* src = p.bank + hoff + cg * 4;
+#pragma unroll
+    for (int j = 0; j < ROWS; ++j) hreg[j] = ld_stream_f4(src + (j * RG + rg) * N);
+  }
   // per-head sums: |k k_k|^2 first (kk needs it)
   float part_nn = wsum(kkr * kkr);
   if (lane == 0) s_dot[warp][3] = part_nn;
