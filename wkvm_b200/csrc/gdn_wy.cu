@@ -622,8 +622,6 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     mma_inflight = false;
     ph_b ^= 1u;
     pend_b = 0;
-    if (tid == 0 && i + 2 < cnt) issue_a(i + 2);  // MMA A has read this buffer
-    if (i + 2 < cnt) pend_a[b] = 1;
     {  // u^T = U^T - (W S)^T ; S^T *= e^(G_C)
       const float* ucol = reinterpret_cast<const float*>(sm + SS_B + (R_U - R_KT)) + v;
       {
@@ -663,8 +661,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     mma_inflight = true;
     if (!wait_all(&mb_m, ph_m)) { failed = true; break; }
     mma_inflight = false;
-    if (tid == 0 && i + 1 < cnt) issue_b(i + 1);  // MMA B has read this buffer
+    // the copy needed next goes out first: U / K~ / A_qk of chunk i+1, then
+    // [W; Q~] of chunk i+2 (MMA A and MMA B have read both buffers)
+    if (tid == 0 && i + 1 < cnt) issue_b(i + 1);
     if (i + 1 < cnt) pend_b = 1;
+    if (tid == 0 && i + 2 < cnt) issue_a(i + 2);
+    if (i + 2 < cnt) pend_a[b] = 1;
   }
 
   if (!failed) {
