@@ -59,9 +59,13 @@ def test_static_scratch_rejects_oversized_batch(cuda):
     # one chunk record and one carried state per (sequence, value head) no
     # longer fit the 64 MiB array
     lib = _lib.load()
+    nseq = 1000
+    # the request must not fit, or the call below would launch on dummy pointers
+    one_window = lib.wkvm_gdn_chunk_workspace_bytes(nseq, 64, 1, 128, 128) + nseq * 128 * 128 * 4
+    assert one_window > 2 * (64 << 20)
     dummy = ctypes.c_void_p(1 << 20)
     rc = lib.wkvm_chunk_gated_delta_rule_static(
-        *([dummy] * 6), None, None, None, 400, 128, 1, 1, 128, 128, ctypes.c_float(1.0), 0, 1,
+        *([dummy] * 6), None, None, None, nseq, 128, 1, 1, 128, 128, ctypes.c_float(1.0), 0, 1,
         None, None)
     assert rc == -10
     assert lib.wkvm_strerror(rc) == b"request larger than the static scratch array"

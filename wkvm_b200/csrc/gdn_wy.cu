@@ -266,10 +266,11 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
       // ---- MMA 1: [k; q] x k^T -> D1 (16-bit operands: the products of
       //      16-bit inputs are exact in the fp32 accumulator)
       if (tid == 0) {
-        const uint32_t x0 = tc::smem_u32(sg + ST_QK);
+        const uint64_t x0 = tc::smem_desc(tc::smem_u32(sg + ST_QK), LBO, SBO_H);
+#pragma unroll
         for (int kk = 0; kk < KD / 16; ++kk)
-          tc::mma_f16(tm + T_D1, tc::smem_desc(x0 + kk * KSTEP, LBO, SBO_H),
-                      tc::smem_desc(x0 + kk * KSTEP, LBO, SBO_H), id_gram, kk > 0);
+          tc::mma_f16(tm + T_D1, tc::desc_add(x0, kk * KSTEP), tc::desc_add(x0, kk * KSTEP),
+                      id_gram, kk > 0);
         tc::mma_commit(&mbar);
       }
       {  // squared norms per row (thread: half a row)
@@ -382,13 +383,13 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
 
       // ---- MMA S: (beta v)^T T^T = U^T -> D1 ; (beta e^G k^)^T T^T = W^T -> DW
       if (tid == 0) {
-        const uint32_t t0 = tc::smem_u32(sg + WS_TT);
+        const uint64_t t0 = tc::smem_desc(tc::smem_u32(sg + WS_TT), LBO, SBO64);
+#pragma unroll
         for (int kk = 0; kk < CH / 8; ++kk)
-          tc::mma_tf32_ta(tm + T_D1, tm + T_AV + kk * 8, tc::smem_desc(t0 + kk * KSTEP, LBO, SBO64),
-                          id_s, kk > 0);
+          tc::mma_tf32_ta(tm + T_D1, tm + T_AV + kk * 8, tc::desc_add(t0, kk * KSTEP), id_s, kk > 0);
+#pragma unroll
         for (int kk = 0; kk < CH / 8; ++kk)
-          tc::mma_tf32_ta(tm + T_DW, tm + T_AK + kk * 8, tc::smem_desc(t0 + kk * KSTEP, LBO, SBO64),
-                          id_s, kk > 0);
+          tc::mma_tf32_ta(tm + T_DW, tm + T_AK + kk * 8, tc::desc_add(t0, kk * KSTEP), id_s, kk > 0);
         tc::mma_commit(&mbar);
       }
       ok = warp != 0 || tc::mbar_wait(&mbar, 1);
@@ -595,11 +596,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     if (tid == 0) {
       ok = tc::mbar_wait(&mb_a[b], ph_a[b]);
       if (ok) {  // MMA A: S^T x [W; Q~]^T
-        const uint32_t a0 = tc::smem_u32(sm + (b ? SS_A1 : SS_A0));
+        const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + (b ? SS_A1 : SS_A0)), LBO, SBO128);
         const uint32_t id = tc::idesc_tf32(128, 128);
+#pragma unroll
         for (int kk = 0; kk < KD / 8; ++kk)
-          tc::mma_tf32_ta(tm + da, tm + T_S + kk * 8, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO128),
-                          id, kk > 0);
+          tc::mma_tf32_ta(tm + da, tm + T_S + kk * 8, tc::desc_add(a0, kk * KSTEP), id, kk > 0);
         tc::mma_commit(&mb_m);
       }
     }
@@ -647,15 +648,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     __syncthreads();
     tc::fence_after_sync();
     if (tid == 0) {  // MMA B: S^T += u^T K~ ; O^T += u^T A_qk^T
-      const uint32_t k0 = tc::smem_u32(sm + SS_B);
-      const uint32_t q0 = k0 + (R_AQK - R_KT);
+      const uint64_t k0 = tc::smem_desc(tc::smem_u32(sm + SS_B), LBO, SBO64);
+      const uint64_t q0 = tc::desc_add(k0, R_AQK - R_KT);
       const uint32_t id128 = tc::idesc_tf32(128, 128), id64 = tc::idesc_tf32(128, 64);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_S, tm + T_U + kk * 8, tc::smem_desc(k0 + kk * KSTEP, LBO, SBO64),
-                        id128, true);
+        tc::mma_tf32_ta(tm + T_S, tm + T_U + kk * 8, tc::desc_add(k0, kk * KSTEP), id128, true);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + da + 64, tm + T_U + kk * 8,
-                        tc::smem_desc(q0 + kk * KSTEP, LBO, SBO64), id64, true);
+        tc::mma_tf32_ta(tm + da + 64, tm + T_U + kk * 8, tc::desc_add(q0, kk * KSTEP), id64, true);
       tc::mma_commit(&mb_m);
     }
     mma_inflight = true;

@@ -32,6 +32,14 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 
+// The descriptor of an operand `bytes` further on in shared memory (the start
+// address field counts 16-byte units; `bytes` keeps it inside the 256 KiB
+// window). MMA issue loops step a base descriptor with this instead of
+// rebuilding one per instruction.
+__device__ __forceinline__ uint64_t desc_add(uint64_t desc, uint32_t bytes) {
+  return desc + (uint64_t)(bytes >> 4);
+}
+
 // Instruction descriptor: D fp32, A and B tf32, both K-major, dense.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) |
