@@ -731,6 +731,10 @@ def run_timemix(args, world, rank, local):
            for _ in range(L)]
     outs = [torch.empty(ACTIVE, D, dtype=torch.bfloat16, device=dev) for _ in range(L)]
     ops.status_word(dev)
+    # Consecutive layers overlap their launch tails (programmatic dependent
+    # launch): each launch touches another layer's state, which meets the
+    # op's contract for the overlap mode.
+    ops.set_decode_overlap(not args.no_overlap)
 
     def step():
         for layer in range(L):
@@ -912,10 +916,15 @@ def run_model_decode(args, world, rank, local):
         # the headline arm: time-mix core fused around the WKV step and the
         # token shift + lerp prologues on the bank's shift rows
         fla_compat.install(fuse_time_mix=True)
+        # The kernel ahead of each time-mix core is a projection GEMM, which
+        # writes neither the arena nor the slot ids: the overlap mode's
+        # contract holds, so the core's launch overlaps that GEMM's tail.
+        prev_overlap = ops.set_decode_overlap(not args.no_overlap)
         clk_ctx = Clocks(dev.index if dev.index is not None else 0)
         with clk_ctx as clk:
             ours_ms = timed(graphed(fused_step))
         ours_eager_ms = timed(fused_step)
+        ops.set_decode_overlap(prev_overlap)
         core_only_ms = timed(graphed(our_step))
         fla_compat.install(fuse_time_mix=False)
         fla_compat.uninstall()
@@ -938,7 +947,9 @@ def run_model_decode(args, world, rank, local):
                                "logits_to_keep=1",
                    "global_batch": ACTIVE * world},
         "path": "fla model; fused time-mix decode core (gates, norms, WKV, GroupNorm, "
-                "correction) and token-shift + lerp prologues on the arena rows",
+                "correction) and token-shift + lerp prologues on the arena rows"
+                + ("" if args.no_overlap else "; time-mix core launched with programmatic "
+                   "dependent launch"),
         "eager_ms_per_step": round(ours_eager_ms, 4),
         "ops_only": {"ms_per_step": round(ops_only_ms, 4),
                      "eager_ms_per_step": round(ops_only_eager_ms, 4),

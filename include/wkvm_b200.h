@@ -107,14 +107,15 @@ int wkvm_wkv7_decode_slots(
     int32_t dtype, int32_t* status, wkvm_stream_t stream);
 
 /* Opt-in (process-wide, off by default) overlap of consecutive
- * wkvm_wkv7_decode_slots launches with programmatic dependent launch: a
- * launch's CTAs may start while the previous kernel in the stream drains,
- * read their slot ids and state, and only then wait for it before reading
- * their inputs. Contract while enabled: the kernel launched immediately
- * before a decode call on the same stream does not write that call's slot
- * ids or those slots' rows of that layer (true for a loop over layers,
- * where each launch touches another layer). Returns the previous setting.
- * No counterpart in the reference. */
+ * wkvm_wkv7_decode_slots and wkvm_wkv7_timemix_decode_slots launches with
+ * programmatic dependent launch: a launch's CTAs may start while the
+ * previous kernel in the stream drains, read their slot ids and state, and
+ * only then wait for it before reading their inputs. Contract while
+ * enabled: the kernel launched immediately before such a call on the same
+ * stream does not write that call's slot ids or those slots' rows of that
+ * layer (true for a loop over layers, where each launch touches another
+ * layer, and for a projection GEMM ahead of the time-mix core). Returns the
+ * previous setting. No counterpart in the reference. */
 int wkvm_set_decode_overlap(int32_t enable);
 
 /* Token-shift + lerp prologue of RWKV-7 single-token decode, with the

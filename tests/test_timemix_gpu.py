@@ -152,3 +152,60 @@ def test_fused_time_mix_model_decode_close_to_fla(cuda, shift_in_bank):
     assert rel_err(ours.shift[:, :, slots], ref.shift[:, :, slots]) < 3e-2
     rest = [i for i in range(5) if i not in slots]
     assert torch.equal(ours.shift[:, :, rest], ref.shift[:, :, rest])
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_timemix_overlap_layer_loop(cuda, graph):
+    """Overlapped (programmatic dependent launch) time-mix over a layer loop
+    whose activations each come from the kernel launched just before (a
+    stand-in for the projection GEMM): the same bits as without overlap,
+    eagerly and inside a CUDA graph."""
+    torch.manual_seed(3)
+    L, S, H, N, B, steps = 4, 9, 4, 64, 5, 3
+    D = H * N
+    mk = lambda *s, sc=1.0: torch.randn(*s, device=cuda) * sc
+    base = [[mk(B, D).to(torch.bfloat16) for _ in range(8)] for _ in range(L)]
+    prm = [[mk(D, sc=0.5).to(torch.bfloat16), mk(D, sc=0.5).to(torch.bfloat16),
+            mk(H, N, sc=0.5).to(torch.bfloat16), mk(D, sc=0.3).to(torch.bfloat16),
+            mk(D, sc=0.1).to(torch.bfloat16)] for _ in range(L)]
+    ids = ops.slot_ids_tensor([5, 1, 7, 3, 8], S, cuda)
+    bank0 = mk(L, S, H, N, N, sc=0.1)
+    acts = [[torch.empty_like(t) for t in base[layer]] for layer in range(L)]
+    outs = [torch.empty(B, D, dtype=torch.bfloat16, device=cuda) for _ in range(L)]
+
+    def run(bank):
+        for s in range(steps):
+            for layer in range(L):
+                a = acts[layer]
+                torch.mul(base[layer][0], 1.0 + s, out=a[0])  # written by the kernel just before
+                for i in range(1, 8):
+                    a[i].copy_(base[layer][i])
+                r, w, k, v, vf, vr, aa, g = a
+                ops.wkv7_timemix_decode_slots(r, w, k, v, vf if layer else None,
+                                              vr if layer else None, aa, g, *prm[layer], 64e-5,
+                                              bank, layer, ids, out=outs[layer])
+        return [o.clone() for o in outs]
+
+    bank_ref = bank0.clone()
+    ref = run(bank_ref)
+    torch.cuda.synchronize()
+    bank = bank0.clone()
+    prev = ops.set_decode_overlap(True)
+    try:
+        if graph:
+            s = torch.cuda.Stream(cuda)
+            s.wait_stream(torch.cuda.current_stream(cuda))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                got = run(bank)
+            bank.copy_(bank0)
+            g.replay()
+        else:
+            got = run(bank)
+        torch.cuda.synchronize()
+    finally:
+        ops.set_decode_overlap(prev)
+    ops.check_device_status(cuda)
+    assert torch.equal(bank, bank_ref)
+    for o, r in zip(got, ref):
+        assert torch.equal(o, r)

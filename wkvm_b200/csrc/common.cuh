@@ -49,6 +49,10 @@ __device__ __forceinline__ void report(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// Process-wide opt-in (wkvm_set_decode_overlap) for programmatic dependent
+// launch of the single-token decode kernels.
+bool decode_overlap();
+
 }  // namespace wkvm
 
 #define WKVM_CUDA_TRY(expr)                         \

@@ -486,6 +486,9 @@ int check_common(const RecArgs& a, bool has_cu) {
 }
 
 }  // namespace
+
+bool decode_overlap() { return g_decode_overlap; }
+
 }  // namespace wkvm
 
 using wkvm::RecArgs;

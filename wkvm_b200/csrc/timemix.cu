@@ -20,6 +20,7 @@ namespace wkvm {
 namespace {
 
 constexpr int N = 64, ROWS = 16, CG = N / 4, RG = N / ROWS, NT = CG * RG;  // 64 threads
+constexpr int kPreRows = 1;  // state rows a thread loads before an overlapped launch's wait
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
@@ -45,6 +46,7 @@ struct TmArgs {
   int H;
   float gn_eps;
   int* status;
+  bool overlap;  // launched with programmatic dependent launch
 };
 
 template <typename T>
@@ -63,6 +65,24 @@ __global__ void __launch_bounds__(NT) wkv7_timemix_decode_kernel(TmArgs p) {
     return;
   }
   const int64_t hoff = ((int64_t)id * H + hh) * (N * N);
+  float4 hreg[ROWS];
+  auto load_state = [&](int j0, int j1) {
+    const float* src = p.bank + hoff + cg * 4;
+#pragma unroll
+    for (int j = 0; j < ROWS; ++j)
+      if (j >= j0 && j < j1) hreg[j] = ld_stream_f4(src + (j * RG + rg) * N);
+  };
+  if (p.overlap) {
+    // Overlapped launch: the CTA starts while the previous kernel in the
+    // stream drains, sends out its first state row (which that kernel does
+    // not write, by the opt-in's contract) and waits; the activations that
+    // kernel may have produced are read after the wait, ahead of the other
+    // state rows. More state before the wait delays the activations (the
+    // gates are the first dependent chain) by more than it gains.
+    load_state(0, kPreRows);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
 
   // ---- staging: thread e = tid owns channel e of this head
   const int64_t base = ((int64_t)n * H + hh) * N + tid;
@@ -85,14 +105,9 @@ __global__ void __launch_bounds__(NT) wkv7_timemix_decode_kernel(TmArgs p) {
   s_ep[0][tid] = to_f32(static_cast<const T*>(p.g)[base]);
   s_ep[1][tid] = to_f32(static_cast<const T*>(p.gn_w)[ch]);
   s_ep[2][tid] = to_f32(static_cast<const T*>(p.gn_b)[ch]);
-  // the state loads go out after the activation loads they would otherwise
+  // otherwise the state loads go out after the activation loads they would
   // delay (the gates below are the first dependent chain)
-  float4 hreg[ROWS];
-  {
-    const float* src = p.bank + hoff + cg * 4;
-#pragma unroll
-    for (int j = 0; j < ROWS; ++j) hreg[j] = ld_stream_f4(src + (j * RG + rg) * N);
-  }
+  load_state(p.overlap ? kPreRows : 0, ROWS);
   // per-head sums: |k k_k|^2 first (kk needs it)
   float part_nn = wsum(kkr * kkr);
   if (lane == 0) s_dot[warp][3] = part_nn;
@@ -200,22 +215,30 @@ extern "C" int wkvm_wkv7_timemix_decode_slots(
   if ((v_first == nullptr) != (v_raw == nullptr)) return WKVM_ERR_INVALID_ARG;
   if (K != wkvm::N) return WKVM_ERR_SHAPE;
   if (reinterpret_cast<uintptr_t>(bank_layer) & 15u) return WKVM_ERR_ALIGN;
+  const bool overlap = wkvm::decode_overlap();
   wkvm::TmArgs a{r, w_raw, k, v, v_first, v_raw, a_raw, g, k_k, k_a, r_k, gn_w, gn_b,
-                 o, bank_layer, slot_ids, num_slots, H, gn_eps, status};
+                 o, bank_layer, slot_ids, num_slots, H, gn_eps, status, overlap};
+  void (*kern)(wkvm::TmArgs);
+  switch (dtype) {
+    case WKVM_DTYPE_BF16: kern = wkvm::wkv7_timemix_decode_kernel<__nv_bfloat16>; break;
+    case WKVM_DTYPE_F16: kern = wkvm::wkv7_timemix_decode_kernel<__half>; break;
+    case WKVM_DTYPE_F32: kern = wkvm::wkv7_timemix_decode_kernel<float>; break;
+    default: return WKVM_ERR_DTYPE;
+  }
   const dim3 grid((unsigned)((int64_t)B * H));
   cudaStream_t st = (cudaStream_t)stream;
-  switch (dtype) {
-    case WKVM_DTYPE_BF16:
-      wkvm::wkv7_timemix_decode_kernel<__nv_bfloat16><<<grid, wkvm::NT, 0, st>>>(a);
-      break;
-    case WKVM_DTYPE_F16:
-      wkvm::wkv7_timemix_decode_kernel<__half><<<grid, wkvm::NT, 0, st>>>(a);
-      break;
-    case WKVM_DTYPE_F32:
-      wkvm::wkv7_timemix_decode_kernel<float><<<grid, wkvm::NT, 0, st>>>(a);
-      break;
-    default:
-      return WKVM_ERR_DTYPE;
+  if (overlap) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(wkvm::NT);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess ? WKVM_OK : WKVM_ERR_CUDA;
   }
+  kern<<<grid, wkvm::NT, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? WKVM_OK : WKVM_ERR_CUDA;
 }
