@@ -356,10 +356,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
 
     // ---- MMA 1: [a~; r~](TMEM) x [k~; b~]^T -> D1
     if (tid == 0) {
-      const uint32_t b0 = tc::smem_u32(sm + S_RB);
+      const uint64_t b0 = tc::smem_desc(tc::smem_u32(sm + S_RB), LBO, SBO);
+#pragma unroll
       for (int kk = 0; kk < HD / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_D1, tm + T_A1 + kk * 8,
-                        tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), idesc128, kk > 0);
+        tc::mma_tf32_ta(tm + T_D1, tm + T_A1 + kk * 8, tc::desc_add(b0, kk * KSTEP), idesc128,
+                        kk > 0);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
@@ -399,10 +400,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     // ---- MMA 2: V^T x A_ak^T -> T_A1 lanes v = (A_ak V)^T. The A operand's
     //      rows 64..127 run into the next tile (S^T) and give unused rows.
     if (tid == 0) {
-      const uint32_t a0 = tc::smem_u32(sm + S_VT), b0 = tc::smem_u32(sm + S_AK);
+      const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + S_VT), LBO, SBO);
+      const uint64_t b0 = tc::smem_desc(tc::smem_u32(sm + S_AK), LBO, SBO);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32(tm + T_A1, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO),
-                     tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
+        tc::mma_tf32(tm + T_A1, tc::desc_add(a0, kk * KSTEP), tc::desc_add(b0, kk * KSTEP),
+                     idesc64, kk > 0);
       tc::mma_commit(&mbar);
     }
 
@@ -461,10 +464,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
 
     // ---- MMA S: [(A_ak V)^T; (a e^Gx)^T] x T^T -> T_D3 = [U~^T; W^T]
     if (tid == 0) {
-      const uint32_t b0 = tc::smem_u32(sm + S_TT);
+      const uint64_t b0 = tc::smem_desc(tc::smem_u32(sm + S_TT), LBO, SBO);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_D3, tm + T_A1 + kk * 8,
-                        tc::smem_desc(b0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
+        tc::mma_tf32_ta(tm + T_D3, tm + T_A1 + kk * 8, tc::desc_add(b0, kk * KSTEP), idesc64,
+                        kk > 0);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
@@ -484,15 +488,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
       const uint32_t w0 = tc::smem_u32(sm + S_RB);
       const uint32_t u0 = w0 + 8 * SBO;
       const uint32_t v0 = tc::smem_u32(sm + S_VT);
+      const uint64_t wd = tc::smem_desc(w0, LBO, SBO), ud = tc::smem_desc(u0, LBO, SBO);
+      const uint64_t vd = tc::smem_desc(v0, LBO, SBO);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_A1, tm + T_D1 + 64 + kk * 8,
-                        tc::smem_desc(w0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
+        tc::mma_tf32_ta(tm + T_A1, tm + T_D1 + 64 + kk * 8, tc::desc_add(wd, kk * KSTEP), idesc64,
+                        kk > 0);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_D3, tm + T_D1 + 64 + kk * 8,
-                        tc::smem_desc(u0 + kk * KSTEP, LBO, SBO), idesc64, kk > 0);
+        tc::mma_tf32_ta(tm + T_D3, tm + T_D1 + 64 + kk * 8, tc::desc_add(ud, kk * KSTEP), idesc64,
+                        kk > 0);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_D3, tm + T_D1 + kk * 8,
-                        tc::smem_desc(v0 + kk * KSTEP, LBO, SBO), idesc64, true);
+        tc::mma_tf32_ta(tm + T_D3, tm + T_D1 + kk * 8, tc::desc_add(vd, kk * KSTEP), idesc64,
+                        true);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
@@ -520,10 +529,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
 
     // ---- MMA 4: [S'; O] = [M; P] x S + [N; O_intra]
     if (tid == 0) {
-      const uint32_t s0 = tc::smem_u32(sm + S_ST);
+      const uint64_t s0 = tc::smem_desc(tc::smem_u32(sm + S_ST), LBO_S, SBO_S);
+#pragma unroll
       for (int kk = 0; kk < HD / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_D3, tm + T_A1 + kk * 8,
-                        tc::smem_desc(s0 + kk * 2 * LBO_S, LBO_S, SBO_S), idesc64, true);
+        tc::mma_tf32_ta(tm + T_D3, tm + T_A1 + kk * 8, tc::desc_add(s0, kk * 2 * LBO_S), idesc64,
+                        true);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
