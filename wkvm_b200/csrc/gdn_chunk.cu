@@ -302,10 +302,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_chunk_kernel(GdnArgs p) {
 
     // ---- MMA 1: [k^; q^] x k^^T -> T_D1 (Gram blocks)
     if (tid == 0) {
-      const uint32_t b0 = tc::smem_u32(sm + S_KB);
+      const uint64_t b0 = tc::smem_desc(tc::smem_u32(sm + S_KB), LBO, SBO128);
+#pragma unroll
       for (int kk = 0; kk < KD / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_D1, tm + T_X1 + kk * 8, tc::smem_desc(b0 + kk * KSTEP, LBO, SBO128),
-                        id64, kk > 0);
+        tc::mma_tf32_ta(tm + T_D1, tm + T_X1 + kk * 8, tc::desc_add(b0, kk * KSTEP), id64, kk > 0);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
@@ -347,10 +347,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_chunk_kernel(GdnArgs p) {
     // ---- MMA 2: V^T x A_ak^T -> T_AKV lanes v (rows 64..127 of A read into
     //      the A_ak tile and give unused rows)
     if (tid == 0) {
-      const uint32_t a0 = tc::smem_u32(sm + S_VT), b0 = tc::smem_u32(sm + S_AK);
+      const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + S_VT), LBO, SBO64);
+      const uint64_t b0 = tc::smem_desc(tc::smem_u32(sm + S_AK), LBO, SBO64);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32(tm + T_AKV, tc::smem_desc(a0 + kk * KSTEP, LBO, SBO64),
-                     tc::smem_desc(b0 + kk * KSTEP, LBO, SBO64), id64, kk > 0);
+        tc::mma_tf32(tm + T_AKV, tc::desc_add(a0, kk * KSTEP), tc::desc_add(b0, kk * KSTEP), id64,
+                     kk > 0);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
@@ -382,13 +384,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_chunk_kernel(GdnArgs p) {
 
     // ---- MMA S: (A_ak V)^T T^T -> U~^T ; (k^ e^Gx)^T T^T -> W^T
     if (tid == 0) {
-      const uint32_t b0 = tc::smem_u32(sm + S_TT);
+      const uint64_t b0 = tc::smem_desc(tc::smem_u32(sm + S_TT), LBO, SBO64);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_U, tm + T_AKV + kk * 8, tc::smem_desc(b0 + kk * KSTEP, LBO, SBO64),
-                        id64, kk > 0);
+        tc::mma_tf32_ta(tm + T_U, tm + T_AKV + kk * 8, tc::desc_add(b0, kk * KSTEP), id64, kk > 0);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_W, tm + T_AG + kk * 8, tc::smem_desc(b0 + kk * KSTEP, LBO, SBO64),
-                        id64, kk > 0);
+        tc::mma_tf32_ta(tm + T_W, tm + T_AG + kk * 8, tc::desc_add(b0, kk * KSTEP), id64, kk > 0);
       tc::mma_commit(&mbar);
     }
     if (!wait_mma()) { failed = true; break; }
@@ -450,10 +452,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_chunk_kernel(GdnArgs p) {
 
     // ---- MMA 3: M += Kh^T W' ; N = Kh^T U' ; P += A_qk W' ; O_intra = A_qk U'
     if (tid == 0) {
-      const uint32_t w0 = tc::smem_u32(sm + S_KB), u0 = tc::smem_u32(sm + S_UPT);
+      const uint64_t w0 = tc::smem_desc(tc::smem_u32(sm + S_KB), LBO, SBO64);
+      const uint64_t u0 = tc::smem_desc(tc::smem_u32(sm + S_UPT), LBO, SBO64);
+#pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk) {
-        const uint64_t wd = tc::smem_desc(w0 + kk * KSTEP, LBO, SBO64);
-        const uint64_t ud = tc::smem_desc(u0 + kk * KSTEP, LBO, SBO64);
+        const uint64_t wd = tc::desc_add(w0, kk * KSTEP);
+        const uint64_t ud = tc::desc_add(u0, kk * KSTEP);
         tc::mma_tf32_ta(tm + T_W, tm + T_X1 + kk * 8, wd, id128, true);
         tc::mma_tf32_ta(tm + T_U, tm + T_X1 + kk * 8, ud, id64, kk > 0);
         tc::mma_tf32_ta(tm + T_AKV, tm + T_D1 + kk * 8, wd, id128, true);
@@ -465,9 +469,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_chunk_kernel(GdnArgs p) {
 
     // ---- MMA 4: S' = M S + N ; O = P S + O_intra
     if (tid == 0) {
-      const uint32_t s0 = tc::smem_u32(sm + S_ST);
+      const uint64_t s0 = tc::smem_desc(tc::smem_u32(sm + S_ST), LBO_S, SBO_S);
+#pragma unroll
       for (int kk = 0; kk < KD / 8; ++kk) {
-        const uint64_t sd = tc::smem_desc(s0 + kk * 2 * LBO_S, LBO_S, SBO_S);
+        const uint64_t sd = tc::desc_add(s0, kk * 2 * LBO_S);
         tc::mma_tf32_ta(tm + T_U, tm + T_W + kk * 8, sd, id64, true);
         tc::mma_tf32_ta(tm + T_O, tm + T_AKV + kk * 8, sd, id64, true);
       }
