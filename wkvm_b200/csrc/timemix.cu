@@ -105,8 +105,8 @@ __global__ void __launch_bounds__(NT) wkv7_timemix_decode_kernel(TmArgs p) {
   s_ep[0][tid] = to_f32(static_cast<const T*>(p.g)[base]);
   s_ep[1][tid] = to_f32(static_cast<const T*>(p.gn_w)[ch]);
   s_ep[2][tid] = to_f32(static_cast<const T*>(p.gn_b)[ch]);
-  // otherwise the state loads go out after the activation loads they would
-  // delay (the gates below are the first dependent chain)
+  // the (remaining) state rows go out after the activation loads they would
+  // otherwise delay (the gates below are the first dependent chain)
   load_state(p.overlap ? kPreRows : 0, ROWS);
   // per-head sums: |k k_k|^2 first (kk needs it)
   float part_nn = wsum(kkr * kkr);
