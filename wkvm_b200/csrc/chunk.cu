@@ -458,9 +458,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
       break;
     }
     tc::fence_after_sync();
-    // The staged inputs and G are spent: stage the next chunk now so its
-    // copies overlap the rest of this one.
-    if (c + 1 < nchunks) stage(c + 1);
 
     // ---- MMA S: [(A_ak V)^T; (a e^Gx)^T] x T^T -> T_D3 = [U~^T; W^T]
     if (tid == 0) {
@@ -471,6 +468,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
                         kk > 0);
       tc::mma_commit(&mbar);
     }
+    // The staged inputs and G are spent: stage the next chunk now so its
+    // copies overlap the rest of this one (after MMA S is issued, so that the
+    // issuing thread does not queue behind its share of the copies).
+    if (c + 1 < nchunks) stage(c + 1);
     if (!wait_mma()) { failed = true; break; }
     {  // [W^T; U~^T] B tile: lane l < 64 holds U~^T row l, lane 64+j holds W^T row j
       float x[CW];
