@@ -447,8 +447,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_chunk_kernel(GdnArgs p) {
       tc::tmem_st_wait();
     }
     sync_tc();
-    // staged q/k/v are spent: stage the next chunk
-    if (c + 1 < nchunks) stage(c + 1);
 
     // ---- MMA 3: M += Kh^T W' ; N = Kh^T U' ; P += A_qk W' ; O_intra = A_qk U'
     if (tid == 0) {
@@ -465,6 +463,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_chunk_kernel(GdnArgs p) {
       }
       tc::mma_commit(&mbar);
     }
+    // staged q/k/v are spent: stage the next chunk (after MMA 3 is issued, so
+    // that the issuing thread does not queue behind its share of the copies)
+    if (c + 1 < nchunks) stage(c + 1);
     if (!wait_mma()) { failed = true; break; }
 
     // ---- MMA 4: S' = M S + N ; O = P S + O_intra
