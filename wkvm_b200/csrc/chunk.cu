@@ -409,19 +409,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
       tc::mma_commit(&mbar);
     }
 
-    // ---- threads 0..255: T = (I - A_ab)^-1 as a K-major tile (row t', K = t),
-    //      while MMA 2 runs; threads 256..511, the column phase (thread =
+    // ---- threads 256..511: T = (I - A_ab)^-1 as a K-major tile (row t',
+    //      K = t), while MMA 2 runs; threads 0..255, the column phase (thread =
     //      column k, 32 tokens): lo lanes Kh^T, Bh^T -> TMEM lanes k of D1's
     //      halves (A_ak, A_ab spent) at once; hi lanes, once MMA 2 is done,
     //      (a e^Gx)^T -> T_A1 lanes 64+k, under (A_ak V)^T in lanes 0..63.
+    //      The inverse is the longer of the two, so it goes to the warps that
+    //      did not just issue MMA 2.
     bool ok2 = true;
-    if (tid < 256) {
-      chunkc::tri_inverse64(Aab, reinterpret_cast<float*>(sm + S_TR), sm + S_TT, tid, 256);
+    if (tid >= 256) {
+      chunkc::tri_inverse64(Aab, reinterpret_cast<float*>(sm + S_TR), sm + S_TT, tid - 256, 256);
     } else if (!lo && !(ok2 = tc::mbar_wait(&mbar, phase))) {
       // reported below (only the hi lanes write where MMA 2 writes)
     } else {
       tc::fence_after_sync();
-      const int k = r64, cc0 = ((warp >> 2) - 2) * 32;
+      const int k = r64, cc0 = (warp >> 2) * 32;
       if (lo) {  // two halves of 16 tokens keep the live registers down
         const float gc = Grow[63 * RS + k];
 #pragma unroll
