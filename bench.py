@@ -359,8 +359,6 @@ def run_prefill(args, world, rank, local):
     token_heads = B * T * H
     flops = token_heads * 109.2e3          # WY-form FLOPs per token-head (N = 64, C = 64)
     byts = token_heads * 896 + 2 * B * H * N * N * 4
-    d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    tf32_peak = d.get("bf16_tflops", 1590.0) / 2  # tf32 dense = half the bf16 rate
     hbm_peak, _ = peaks()
     return {
         "metric": "WKV-7 chunked prefill tokens/s (BASELINE config 2)",
@@ -374,11 +372,28 @@ def run_prefill(args, world, rank, local):
         "roofline": {"bound": "hbm", "achieved": round(byts / (step_ms * 1e-3) / 1e9, 1),
                      "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(byts / (step_ms * 1e-3) / 1e9 / hbm_peak, 4),
-                     "tensor_tflops": round(flops / (step_ms * 1e-3) / 1e12, 2),
-                     "tensor_peak_tflops": tf32_peak,
-                     "tensor_peak_kind": "measured bf16_tflops / 2 (tf32 dense rate)"},
+                     "bytes_per_launch": int(byts), "flops_per_launch": int(flops),
+                     **tensor_roof(flops, step_ms)},
         "clocks": clk.summary(), "gpu_launches": args.steps,
     }
+
+
+def tensor_roof(flops: float, ms: float) -> dict:
+    """Tensor-pipe figures of a tf32 tensor-core launch: achieved TFLOP/s
+    against the tf32 dense rate, taken as half the measured bf16 GEMM rate,
+    burst (the kernel timed alone) and sustained (under the power cap)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    d = json.loads(p.read_text()) if p.exists() else {}
+    kind = "measured" if d else "fallback"
+    burst = d.get("bf16_tflops", 1590.0) / 2
+    sustained = d.get("bf16_tflops_sustained", 1400.0) / 2
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"tensor_tflops": round(tf, 2), "tensor_peak_tflops": burst,
+            "tensor_frac": round(tf / burst, 4),
+            "tensor_peak_sustained_tflops": sustained,
+            "tensor_frac_sustained": round(tf / sustained, 4),
+            "tensor_peak_kind": f"{kind} bf16_tflops / 2 and bf16_tflops_sustained / 2 "
+                                "(tf32 dense rate)"}
 
 
 def run_gdn(args, world, rank, local):
@@ -434,13 +449,11 @@ def run_gdn(args, world, rank, local):
         kernel = "gdn_recurrent_kernel<128,128,16> (gdn_decode_slots)"
     else:
         byts = th * 1028 + 2 * B * HG * K * K * 4
-        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
         line_roof = {"bound": "hbm", "achieved": round(byts / (step_ms * 1e-3) / 1e9, 1),
                      "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(byts / (step_ms * 1e-3) / 1e9 / hbm_peak, 4),
-                     "tensor_tflops": round(th * 183e3 / (step_ms * 1e-3) / 1e12, 2),
-                     "tensor_peak_tflops": d.get("bf16_tflops", 1590.0) / 2,
-                     "tensor_peak_kind": "measured bf16_tflops / 2 (tf32 dense rate)"}
+                     "peak_kind": f"{kind} hbm_gbs", "bytes_per_launch": int(byts),
+                     "flops_per_launch": int(th * 183e3), **tensor_roof(th * 183e3, step_ms)}
         from wkvm_b200 import _lib
         line_roof["workspace_bytes_per_step"] = int(
             _lib.load().wkvm_gdn_chunk_workspace_bytes(B, T, HG, K, K))
@@ -1022,6 +1035,25 @@ def run_reference(args, world, rank):
     }
 
 
+def side_workloads(args, world, rank, local):
+    """BASELINE configs 2 and 3 timed in the same run as the headline decode
+    line (1 GPU): RWKV-7 chunked prefill, GDN decode and GDN chunked prefill,
+    each with its own CUDA-event timing, roofline and clock record."""
+    import copy
+    out = {}
+    for name, wl, fn in (("cfg2_wkv7_prefill", "prefill", run_prefill),
+                         ("cfg3_gdn_decode", "gdn-decode", run_gdn),
+                         ("cfg3_gdn_prefill", "gdn-prefill", run_gdn)):
+        a = copy.copy(args)
+        a.workload = wl
+        r = fn(a, world, rank, local)
+        torch.cuda.empty_cache()
+        out[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
+                                       "warmup", "config", "roofline", "clocks",
+                                       "gpu_launches")}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1031,6 +1063,8 @@ def main():
     ap.add_argument("--cpu-sample-slots", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="skip the config 2 / 3 lines the default 1-GPU run adds")
     ap.add_argument("--no-overlap", action="store_true",
                     help="plain launches instead of programmatic dependent launch")
     ap.add_argument("--layers", type=int, default=24,
@@ -1066,6 +1100,8 @@ def main():
             line = run_timemix(args, world, rank, local)
         else:
             line = run_ours(args, world, rank, local)
+            if world == 1 and not args.no_workloads:
+                line["workloads"] = side_workloads(args, world, rank, local)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()

@@ -110,7 +110,9 @@ int wkvm_wkv7_decode_slots(
  * wkvm_wkv7_decode_slots and wkvm_wkv7_timemix_decode_slots launches with
  * programmatic dependent launch: a launch's CTAs may start while the
  * previous kernel in the stream drains, read their slot ids and state, and
- * only then wait for it before reading their inputs. Contract while
+ * only then wait for it before reading their inputs. A launch lets the
+ * next one start only after its own wait has returned, so a launch never
+ * runs beside any kernel older than its immediate predecessor. Contract while
  * enabled: the kernel launched immediately before such a call on the same
  * stream does not write that call's slot ids or those slots' rows of that
  * layer (true for a loop over layers, where each launch touches another
@@ -264,9 +266,9 @@ int64_t wkvm_gdn_chunk_workspace_bytes(int32_t nseq, int32_t T, int32_t HV, int3
  * 16-bit inputs only (WKVM_ERR_SHAPE / WKVM_ERR_DTYPE otherwise). Longer
  * inputs run in windows of chunks; WKVM_ERR_SCRATCH when even one window
  * does not fit (about nseq * HV > 300). Runs on the current device; the
- * first call on each device looks up the array's device address
- * (cudaGetSymbolAddress), so make that first call before any stream
- * capture. All calls share the array: calls that overlap on the GPU (other
+ * first call on each device, and the first after a cudaDeviceReset, looks
+ * up the array's device address (cudaGetSymbolAddress), so make that first
+ * call before any stream capture. All calls share the array: calls that overlap on the GPU (other
  * streams, other host threads) race; sequential calls need nothing cleared
  * between them, since each call writes every byte it reads. */
 int wkvm_chunk_gated_delta_rule_static(

@@ -9,27 +9,38 @@ ROOT = Path(__file__).resolve().parents[1]
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
-# Parity tolerance against the fp32 oracle: max |x - y| / max |y| over the
-# tensor. fp32 tensors (states, fp32 outputs) must meet REL_TOL itself. A
-# bf16/fp16 output additionally carries its own rounding (a bf16 value is
-# within 2^-8 of the fp32 value it rounds, relative to that value), so its
-# bound is REL_TOL + that rounding, and its mean error must meet REL_TOL.
+# Parity tolerance against the fp32 oracle (the 2e-3 of the spec).
+# fp32 tensors (states, fp32 outputs): max |x - y| / max |y| < REL_TOL.
+# 16-bit outputs are checked element by element:
+#     |x_i - y_i| <= REL_TOL * max|y| + U * |y_i|
+# i.e. the same 2e-3 of the tensor's scale plus the rounding of x_i itself to
+# its dtype: U is the unit roundoff (half an ulp, relative), 2^-8 for bf16
+# (7 stored fraction bits) and 2^-11 for fp16 (10 bits). An fp32 result that
+# meets 2e-3 meets this bound after rounding, whatever the element's size.
 REL_TOL = 2e-3
 ROUNDING = {torch.bfloat16: 2.0 ** -8, torch.float16: 2.0 ** -11, torch.float32: 0.0}
 
 
-def out_tol(t: torch.Tensor) -> float:
-    return REL_TOL + ROUNDING[t.dtype]
+def out_excess(x: torch.Tensor, y) -> float:
+    """max_i |x_i - y_i| / (REL_TOL * max|y| + U * |y_i|): < 1 passes."""
+    u = ROUNDING[x.dtype]
+    xm = np.asarray(x.detach().float().cpu(), np.float64)
+    ym = np.asarray(y.detach().float().cpu() if isinstance(y, torch.Tensor) else y, np.float64)
+    scale = max(np.abs(ym).max(), 1e-30)
+    bound = REL_TOL * scale * (1.0 + u) + u * np.abs(ym)
+    return float((np.abs(xm - ym) / bound).max())
 
 
 def assert_out_close(x: torch.Tensor, y, what="o"):
-    """Output gate: max-relative within out_tol(x), mean-relative within REL_TOL."""
-    e = rel_err(x, y)
-    assert e < out_tol(x), f"{what}: max rel err {e:.3e} >= {out_tol(x):.3e}"
-    xm = np.asarray(x.detach().float().cpu(), np.float64)
-    ym = np.asarray(y.detach().float().cpu() if isinstance(y, torch.Tensor) else y, np.float64)
-    m = np.abs(xm - ym).mean() / max(np.abs(ym).mean(), 1e-30)
-    assert m < REL_TOL, f"{what}: mean rel err {m:.3e}"
+    """Output gate: element-wise 2e-3 of max|y| plus the dtype's own rounding
+    of each element (fp32 outputs: plain max-relative 2e-3)."""
+    if x.dtype == torch.float32:
+        e = rel_err(x, y)
+        assert e < REL_TOL, f"{what}: max rel err {e:.3e} >= {REL_TOL:.1e}"
+        return
+    q = out_excess(x, y)
+    assert q < 1.0, (f"{what}: error reaches {q:.3f} of the element-wise bound "
+                     f"(max rel err {rel_err(x, y):.3e})")
 
 
 def pytest_configure(config):

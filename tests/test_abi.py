@@ -48,15 +48,26 @@ def test_version_and_strerror(lib):
     assert lib.wkvm_strerror(-4) == b"slot id out of range"
 
 
+def _buffers():
+    """Two pointers the rejected calls below receive: zeroed 1 MiB device
+    buffers when a GPU is present (a check that regressed then launches on
+    real memory, larger than any of these calls would touch), else dummy
+    addresses that no call here may dereference."""
+    import torch
+    if torch.cuda.is_available():
+        bufs = [torch.zeros(1 << 20, dtype=torch.uint8, device="cuda") for _ in range(2)]
+        return bufs, [ctypes.c_void_p(b.data_ptr()) for b in bufs]
+    return [], [ctypes.c_void_p(4096), ctypes.c_void_p(1 << 20)]
+
+
 def test_host_argument_checks(lib):
     from wkvm_b200 import _lib
+    keep, (dummy, dummy2) = _buffers()
     # null bank / ids are rejected before anything reaches the device
     assert lib.wkvm_slot_copy(None, 1, 16, 16, 16, 4, None, None, 1, None, None) == -1
     # misaligned row size
-    assert lib.wkvm_slot_zero(ctypes.c_void_p(256), 1, 24, 24, 24, 4, ctypes.c_void_p(512), 1,
-                              None, None) == -7
+    assert lib.wkvm_slot_zero(dummy, 1, 24, 24, 24, 4, dummy2, 1, None, None) == -7
     # unsupported head dim never launches
-    dummy = ctypes.c_void_p(4096)
     rc = lib.wkvm_fused_mul_recurrent_rwkv7(*([dummy] * 7), None, None, None, 1, 1, 1, 48, 48,
                                             ctypes.c_float(1.0), 1, None, None)
     assert rc == -2
@@ -69,6 +80,9 @@ def test_host_argument_checks(lib):
                                     None)
     assert rc == 0
     assert _lib.ERR_NAMES[-5] == "WKVM_ERR_DUPLICATE"
+    if keep:
+        import torch
+        torch.cuda.synchronize()
 
 
 def test_gdn_workspace_size(lib):

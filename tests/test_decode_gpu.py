@@ -171,31 +171,54 @@ def test_gdn_decode_slots_long(cuda):
     assert rel_err(bank[0, ids], rh) < REL_TOL
 
 
-def test_decode_overlap_layer_loop(cuda):
-    """Overlapped (programmatic dependent launch) decode over a layer loop,
-    as a model step issues it, several steps in a row, inside a CUDA graph
-    and eagerly: same results as the oracle run layer by layer."""
-    L, S, H, N, B, steps = 4, 9, 4, 64, 3, 3
+@pytest.mark.parametrize("L", [2, 12])
+@pytest.mark.parametrize("graphed", [True, False])
+def test_decode_overlap_layer_loop(cuda, L, graphed):
+    """Overlapped (programmatic dependent launch) decode over a layer loop at
+    the config-0 shape (B=8, H=12, N=64; L=12, and L=2 where the same layer
+    comes back every other launch), 64 steps launched back to back: either
+    all 64 x L launches captured in one CUDA graph (no gaps between
+    launches, the case where short launches could pile up) or eagerly.
+    Every step's output and the final state match the oracle run layer by
+    layer."""
+    S, H, N, B, steps = 40, 12, 64, 8, 64
     bank = _bank(L, S, H, N, cuda, seed=4)
-    h_ref = [np32(bank[layer, [5, 1, 7]]) for layer in range(L)]
-    ids = ops.slot_ids_tensor([5, 1, 7], S, cuda)
-    xs = [[_to(synth.rwkv7_inputs(B, 1, H, N, seed=100 * s + layer, state=False), cuda)
-           for layer in range(L)] for s in range(steps)]
+    slot_list = synth.slot_ids(B, S, seed=3).long()
+    h_ref = [np32(bank[layer, slot_list]) for layer in range(L)]
+    ids = ops.slot_ids_tensor(slot_list, S, cuda)
+    names = ("r", "w", "k", "v", "kk", "a")
+    # per layer, all steps drawn at once as [B, steps, H, N]; step s is [:, s:s+1]
+    xs = [synth.rwkv7_inputs(B, steps, H, N, seed=1000 + layer, state=False) for layer in range(L)]
+    ds = [_to(x, cuda) for x in xs]
+    step_in = [[[ds[layer][n][:, s:s + 1].contiguous() for n in names] for layer in range(L)]
+               for s in range(steps)]
+    outs = [[torch.empty(B, 1, H, N, dtype=torch.bfloat16, device=cuda) for _ in range(L)]
+            for _ in range(steps)]
+
+    def run():
+        for s in range(steps):
+            for layer in range(L):
+                ops.wkv7_decode_slots(*step_in[s][layer], bank, layer, ids, out=outs[s][layer])
+
+    ops.status_word(cuda)
     prev = ops.set_decode_overlap(True)
     try:
-        outs = []
-        for s in range(steps):
-            outs.append([ops.wkv7_decode_slots(*(xs[s][layer][n] for n in ("r", "w", "k", "v", "kk", "a")),
-                                               bank, layer, ids) for layer in range(L)])
+        if graphed:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                run()
+            bank[:, slot_list] = torch.from_numpy(np.stack(h_ref, 0)).to(cuda)
+            torch.cuda.synchronize()
+            graph.replay()
+        else:
+            run()
         torch.cuda.synchronize()
     finally:
         ops.set_decode_overlap(prev)
     for layer in range(L):
-        h = h_ref[layer]
-        for s in range(steps):
-            x = xs[s][layer]
-            ro, h = oracle.rwkv7_recurrence(*(np32(x[n]) for n in ("r", "w", "k", "v", "kk", "a")),
-                                            initial_state=h)
-            assert_out_close(outs[s][layer], ro)
-        assert rel_err(bank[layer, [5, 1, 7]], h) < REL_TOL
+        x = xs[layer]
+        ro, h = oracle.rwkv7_recurrence(*(np32(x[n]) for n in names), initial_state=h_ref[layer])
+        o = torch.cat([outs[s][layer] for s in range(steps)], 1)
+        assert_out_close(o, ro, what=f"layer {layer}")
+        assert rel_err(bank[layer, slot_list], h) < REL_TOL
     ops.check_device_status(cuda)

@@ -53,3 +53,22 @@ def test_family_geometry_matches_reference_layout():
     outer, ostr, sstr, row, ns = ops._family_geometry(shift, 2)
     assert (outer, ns, row) == (6, 5, 128) and ostr == 5 * 128
     assert lay.wkv_bytes_per_slot() == 3 * 2 * 32 * 32 * 4
+
+
+def test_slot_affine_rejects_chained_pairs():
+    fam = torch.zeros(2, 6, 4)
+    # slot 2 is pair 0's destination and pair 1's source: pairs run at once
+    with pytest.raises(ValueError, match="another pair's source"):
+        ops.slot_affine(fam, 1, [2, 3], [1, 2], None, 0.5)
+    with pytest.raises(ValueError, match="another pair's source"):
+        ops.slot_affine(fam, 1, [4, 5], [1, 2], [5, 3], 0.5, 0.5)
+
+
+def test_debug_checks_toggle():
+    from wkvm_b200 import _lib
+    prev = ops.set_debug_checks(True)
+    try:
+        assert _lib.post_call is not None
+    finally:
+        ops.set_debug_checks(prev)
+    assert (_lib.post_call is None) == (not prev)

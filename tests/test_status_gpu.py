@@ -89,3 +89,23 @@ def test_timemix_bad_id(cuda):
     ops.check_device_status(cuda)
     assert torch.equal(bank, ref)
     assert torch.equal(o[keep], o_ref)
+
+
+def test_debug_checks_raise_at_the_call(cuda):
+    """With ops.set_debug_checks(True) a device id tensor with a duplicate
+    is rejected before the launch, and a device-side error raises from the
+    op that met it instead of waiting for check_device_status."""
+    H, N = 2, 64
+    x = {k: v.to(cuda) for k, v in synth.rwkv7_inputs(3, 1, H, N, seed=7, state=False).items()}
+    bank = torch.randn(1, 6, H, N, N, device=cuda) * 0.1
+    args = [x[n] for n in ("r", "w", "k", "v", "kk", "a")]
+    prev = ops.set_debug_checks(True)
+    try:
+        with pytest.raises(RuntimeError, match="DUPLICATE"):
+            ops.wkv7_decode_slots(*args, bank, 0, _ids([1, 4, 1], cuda))
+        with pytest.raises(RuntimeError, match="SLOT_RANGE"):
+            ops.wkv7_decode_slots(*args, bank, 0, _ids([1, 4, 9], cuda))
+        ops.wkv7_decode_slots(*args, bank, 0, _ids([1, 4, 5], cuda))
+    finally:
+        ops.set_debug_checks(prev)
+    ops.check_device_status(cuda)

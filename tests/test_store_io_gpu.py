@@ -66,3 +66,24 @@ def test_hibernate_into_reused_buffers(cuda):
         assert torch.equal(b.wkv, bank.wkv[:, sess].transpose(0, 1).cpu())
     with pytest.raises(ValueError):
         store_io.hibernate(bank, [1, 2, 3, 4, 5], pool)
+
+
+def test_wake_from_pageable_host_tensors(cuda):
+    """wake() given plain (unpinned) CPU tensors stages each one in pinned
+    memory; every staged copy must outlive the restore that reads it, so
+    several sessions woken in a row all land bit-exact."""
+    lay = RWKV7StateLayout(n_layer=4, hidden_size=128, num_heads=2, head_dim=64, head_v_dim=64)
+    bank = RWKV7StateBank(lay, num_slots=16, device=cuda)
+    g = torch.Generator().manual_seed(11)
+    sessions = [{"wkv": torch.randn(4, 2, 64, 64, generator=g),
+                 "shift": torch.randn(4, 2, 128, generator=g).to(lay.dtype)} for _ in range(8)]
+    assert not sessions[0]["wkv"].is_pinned()
+    slots = [9, 2, 14, 5, 11, 3, 7, 16]
+    store_io.wake(bank, slots, sessions)
+    # whatever the host allocator hands out next must not disturb the result
+    junk = [torch.full((4, 2, 64, 64), 7.0).pin_memory() for _ in range(8)]
+    torch.cuda.synchronize()
+    for s, t in zip(slots, sessions):
+        assert torch.equal(bank.wkv[:, s].cpu(), t["wkv"])
+        assert torch.equal(bank.shift[:, :, s].cpu(), t["shift"])
+    del junk

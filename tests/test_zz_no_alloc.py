@@ -59,13 +59,20 @@ def test_static_scratch_rejects_oversized_batch(cuda):
     # one chunk record and one carried state per (sequence, value head) no
     # longer fit the 64 MiB array
     lib = _lib.load()
-    nseq = 1000
-    # the request must not fit, or the call below would launch on dummy pointers
+    nseq, T = 1000, 128
     one_window = lib.wkvm_gdn_chunk_workspace_bytes(nseq, 64, 1, 128, 128) + nseq * 128 * 128 * 4
     assert one_window > 2 * (64 << 20)
-    dummy = ctypes.c_void_p(1 << 20)
+    # real buffers of the stated shape (about 260 MB), so that a regression in
+    # the size check gives a wrong answer, never an access outside memory
+    x = synth.gdn_inputs(nseq, T, 1, 128, seed=9)
+    d = {n: t.to(cuda) for n, t in x.items()}
+    o = torch.empty_like(d["v"])
+    ht = torch.empty_like(d["h0"])
+    P = ctypes.c_void_p
     rc = lib.wkvm_chunk_gated_delta_rule_static(
-        *([dummy] * 6), None, None, None, nseq, 128, 1, 1, 128, 128, ctypes.c_float(1.0), 0, 1,
-        None, None)
+        *(P(d[n].data_ptr()) for n in GDN), P(o.data_ptr()), P(d["h0"].data_ptr()),
+        P(ht.data_ptr()), None, nseq, T, 1, 1, 128, 128, ctypes.c_float(1.0), 0, 1,
+        None, P(torch.cuda.current_stream(cuda).cuda_stream))
+    torch.cuda.synchronize()
     assert rc == -10
     assert lib.wkvm_strerror(rc) == b"request larger than the static scratch array"

@@ -100,6 +100,11 @@ def load(path: Path | str | None = None):
         return lib
 
 
+# Called with the entry point's name after every successful call when set
+# (wkvm_b200.ops.set_debug_checks installs a device-status check here).
+post_call = None
+
+
 def call(name: str, *args) -> None:
     """Calls an entry point and raises WkvmError on a nonzero return."""
     lib = load()
@@ -107,6 +112,8 @@ def call(name: str, *args) -> None:
     rc = fn(*args)
     if rc != 0:
         raise WkvmError(name, rc)
+    if post_call is not None:
+        post_call(name)
 
 
 def exported_symbols() -> list[str]:

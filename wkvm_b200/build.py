@@ -19,9 +19,6 @@ LIB = PKG / "libwkvm_b200.so"
 SOURCES = ["recurrent.cu", "slots.cu", "selftest.cu", "chunk.cu", "gdn_chunk.cu", "gdn_wy.cu",
            "gdn_static.cu", "timemix.cu", "shift_mix.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CUTLASS_INCLUDE_CANDIDATES = [
-    Path(sys.prefix) / "lib/python3.12/site-packages/flashinfer/data/cutlass/include",
-]
 
 
 def _nvcc() -> str:

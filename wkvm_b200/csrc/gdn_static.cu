@@ -32,18 +32,49 @@ static __device__ __align__(256) uint8_t g_gdn_scratch[kGdnScratchBytes];
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};
+
+// cuCtxGetId of the current context (0 if the driver cannot say), fetched
+// through the runtime so the library needs no link against libcuda.
+using CtxGetCurrentFn = int (*)(void**);
+using CtxGetIdFn = int (*)(void*, unsigned long long*);
+
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    looked_up = true;
+    cudaDriverEntryPointQueryResult q1, q2;
+    void* f1 = nullptr;
+    void* f2 = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) == cudaSuccess &&
+        cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) == cudaSuccess &&
+        q1 == cudaDriverEntryPointSuccess && q2 == cudaDriverEntryPointSuccess) {
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+      get_id = reinterpret_cast<CtxGetIdFn>(f2);
+    }
+  }
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == 0 && ctx) get_id(ctx, &id);
+  return id;
+}
 
 // Device address of g_gdn_scratch on the current device, looked up once per
-// device (the host-side symbol is not a device address).
+// device and context (the host-side symbol is not a device address). A new
+// context on the device (after cudaDeviceReset) is looked up afresh.
 int scratch_address(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return WKVM_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return WKVM_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  const unsigned long long ctx = current_context_id();
+  if (!g_scratch_ptr[dev] || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_gdn_scratch) != cudaSuccess || !p) return WKVM_ERR_CUDA;
     g_scratch_ptr[dev] = p;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_ptr[dev];
   return WKVM_OK;

@@ -134,12 +134,14 @@ wkv7_recurrent_kernel(const Tin* __restrict__ r, const Tin* __restrict__ w,
     nx[5] = x6[b];
   };
   // Programmatic dependent launch (opt-in for decode, see
-  // wkvm_set_decode_overlap): let the next launch in the stream start its
-  // CTAs now, and wait for the previous launch only here, after the slot ids
-  // and the state were read and before any input is. Without the launch
-  // attribute both instructions are no-ops.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // wkvm_set_decode_overlap): the slot ids and the state were read above,
+  // while the previous launch in the stream may still run; wait for it here,
+  // before any input is read. Only after the wait does this CTA let the next
+  // launch start, so at most two launches overlap: a launch can run beside
+  // its immediate predecessor only, never beside an older one. Without the
+  // launch attribute both instructions are no-ops.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid < N && sr.len > 0) fetch(0);
 
   for (int64_t t = 0; t < sr.len; ++t) {

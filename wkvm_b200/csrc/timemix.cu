@@ -78,10 +78,12 @@ __global__ void __launch_bounds__(NT) wkv7_timemix_decode_kernel(TmArgs p) {
     // not write, by the opt-in's contract) and waits; the activations that
     // kernel may have produced are read after the wait, ahead of the other
     // state rows. More state before the wait delays the activations (the
-    // gates are the first dependent chain) by more than it gains.
+    // gates are the first dependent chain) by more than it gains. The next
+    // launch is released only after the wait, so no launch ever runs beside
+    // a kernel older than its immediate predecessor.
     load_state(0, kPreRows);
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   }
 
   // ---- staging: thread e = tid owns channel e of this head

@@ -202,12 +202,18 @@ class SlotCacheHandle:
     rows gathered for this batch; :meth:`commit` writes the updated
     token-shift rows back to the bank."""
 
-    def __init__(self, bank, slot_ids, shift_in_bank: bool = False):
+    def __init__(self, bank, slot_ids, shift_in_bank: bool = False, shift_ids=None):
         from fla.models.utils import Cache
 
         self.bank = bank
         dev = bank.device
         self.ids = ops.slot_ids_tensor(slot_ids, bank.num_slots + 1, dev)
+        # the token-shift family's own slot ids (wkvm's slot dicts name one id
+        # per family); the wkv ids when not given
+        self.shift_ids = (self.ids if shift_ids is None
+                          else ops.slot_ids_tensor(shift_ids, bank.num_slots + 1, dev))
+        if self.shift_ids.numel() != self.ids.numel():
+            raise ValueError("wkv and shift slot id lists differ in length")
         L = bank.layout.n_layer
         self.shift_in_bank = shift_in_bank
         if shift_in_bank:  # the fused prologues read and write bank.shift in place
@@ -215,12 +221,12 @@ class SlotCacheHandle:
             self.cache = Cache()
             for i in range(L):
                 self.cache.update(recurrent_state=SlotState(bank.wkv, i, self.ids),
-                                  conv_state=SlotShift(bank.shift, i, 0, self.ids),
-                                  ffn_state=SlotShift(bank.shift, i, 1, self.ids),
+                                  conv_state=SlotShift(bank.shift, i, 0, self.shift_ids),
+                                  ffn_state=SlotShift(bank.shift, i, 1, self.shift_ids),
                                   layer_idx=i, offset=0)
             return
         # [L, 2, n, D]: one kernel, and every (layer, family) view is contiguous
-        self.shift = ops.slot_gather_outer_major(bank.shift, 2, self.ids)
+        self.shift = ops.slot_gather_outer_major(bank.shift, 2, self.shift_ids)
         self.cache = Cache()
         for i in range(L):
             self.cache.update(recurrent_state=SlotState(bank.wkv, i, self.ids),
@@ -239,12 +245,29 @@ class SlotCacheHandle:
                 x = st[key]
                 if x.data_ptr() == self.shift[i, j].data_ptr():
                     x = self.shift[i, j]
-                ops.slot_restore(self.bank.shift[i, j], 0, self.ids,
+                ops.slot_restore(self.bank.shift[i, j], 0, self.shift_ids,
                                  x.reshape(self.ids.numel(), -1).to(self.bank.shift.dtype))
 
 
-def slot_cache(bank, slot_ids, shift_in_bank: bool = False) -> SlotCacheHandle:
+def slot_cache(bank, slot_ids, shift_in_bank: bool = False, shift_ids=None) -> SlotCacheHandle:
     """fla Cache over the arena rows of ``slot_ids``; see the module docstring
     for ``shift_in_bank`` (single-token decode with install(fuse_time_mix=True)
-    only: fla's own token shift cannot read a SlotShift and raises)."""
-    return SlotCacheHandle(bank, slot_ids, shift_in_bank)
+    only: fla's own token shift cannot read a SlotShift and raises).
+    ``shift_ids`` names the token-shift family's rows when they differ."""
+    return SlotCacheHandle(bank, slot_ids, shift_in_bank, shift_ids)
+
+
+def installed() -> bool:
+    """True while fla's RWKV7Attention runs wkvm_b200's ops (after install())."""
+    if not _orig:
+        return False
+    import fla.layers.rwkv7 as layer
+    return layer.fused_mul_recurrent_rwkv7 is fused_mul_recurrent_rwkv7
+
+
+def fused_installed() -> bool:
+    """True after install(fuse_time_mix=True)."""
+    if not installed():
+        return False
+    import fla.layers.rwkv7 as layer
+    return layer.RWKV7Attention.forward is _fused_time_mix_forward

@@ -70,6 +70,31 @@ def check_device_status(device=None, reset: bool = True) -> None:
         raise _lib.WkvmError("device kernel", code)
 
 
+_debug = False
+
+
+def set_debug_checks(enable: bool) -> bool:
+    """Debug mode (off by default; returns the previous setting). While on,
+    every op synchronises after its launch and raises the first device-side
+    error the kernels recorded (check_device_status on every device used so
+    far), and slot ids given as CUDA tensors are checked for range and
+    duplicates on the host before the launch. Not for use inside CUDA graph
+    capture: it synchronises."""
+    global _debug
+    prev = _debug
+    _debug = bool(enable)
+    _lib.post_call = _check_after_call if _debug else None
+    return prev
+
+
+def _check_after_call(name: str) -> None:
+    for idx in list(_status):
+        code = int(_status[idx].item())
+        if code != 0:
+            _status[idx].zero_()
+            raise _lib.WkvmError(f"{name} (device {idx})", code)
+
+
 def _require_cuda(*ts):
     for t in ts:
         if t is not None and not t.is_cuda:
@@ -268,15 +293,25 @@ def slot_ids_tensor(slot_ids, num_slots: int, device, validate: bool = True) -> 
     if isinstance(slot_ids, torch.Tensor) and slot_ids.is_cuda:
         if slot_ids.dtype != torch.int32:
             slot_ids = slot_ids.to(torch.int32)
-        return slot_ids.contiguous()
+        if not (_debug and validate):
+            return slot_ids.contiguous()
+        dev_ids = slot_ids.contiguous()
+        ids = dev_ids.reshape(-1).to("cpu", torch.int64)
+        _validate_ids(ids, num_slots)
+        return dev_ids
     ids = torch.as_tensor(slot_ids, dtype=torch.int64).reshape(-1)
-    if validate and ids.numel():
+    if validate:
+        _validate_ids(ids, num_slots)
+    return ids.to(torch.int32).to(device, non_blocking=True)
+
+
+def _validate_ids(ids: torch.Tensor, num_slots: int) -> None:
+    if ids.numel():
         lo, hi = int(ids.min()), int(ids.max())
         if lo < 0 or hi >= num_slots:
             raise _lib.WkvmError("slot id check", -4)
         if torch.unique(ids).numel() != ids.numel():
             raise _lib.WkvmError("slot id check", -5)
-    return ids.to(torch.int32).to(device, non_blocking=True)
 
 
 def _bank_layer(bank: torch.Tensor, layer: int) -> torch.Tensor:
@@ -494,6 +529,20 @@ def slot_affine(family: torch.Tensor, slot_dim: int, dst_ids, a_ids, b_ids, c1: 
     b = None if b_ids is None else slot_ids_tensor(b_ids, ns, family.device, validate=False)
     if a.numel() != d.numel() or (b is not None and b.numel() != d.numel()):
         raise ValueError("id lists differ in length")
+    host_lists = [x for x in (dst_ids, a_ids, b_ids)
+                  if x is not None and not (isinstance(x, torch.Tensor) and x.is_cuda)]
+    if len(host_lists) == (3 if b_ids is not None else 2):
+        # pairs run concurrently: a destination may be its own pair's source
+        # (in place) but no other pair's
+        dl = torch.as_tensor(dst_ids).reshape(-1).tolist()
+        srcs = [torch.as_tensor(x).reshape(-1).tolist() for x in (a_ids, b_ids) if x is not None]
+        users: dict[int, set[int]] = {}
+        for src in srcs:
+            for j, sj in enumerate(src):
+                users.setdefault(sj, set()).add(j)
+        for i, di in enumerate(dl):
+            if users.get(di, set()) - {i}:
+                raise ValueError(f"slot {di} is a destination and another pair's source")
     dt = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[family.dtype]
     with torch.cuda.device(family.device):
         _lib.call("wkvm_slot_affine", _ptr(family), outer, ostr, sstr, row, ns, _ptr(d),

@@ -109,27 +109,50 @@ class RWKV7StateBank:
         """Validated int32 device ids for a batch (reuse across layers/steps)."""
         return ops.slot_ids_tensor(_ids(slot_batch, family), self.num_slots + 1, self.device)
 
-    # -- gather / scatter compatibility (wkvm/runner/state.py:63-97) --------
+    # -- gather / scatter (wkvm/runner/state.py:63-97) ----------------------
 
-    def gather_cache(self, slot_batch: Sequence[SlotDict]) -> list[dict[str, torch.Tensor]]:
-        """Per-layer dicts of gathered copies with fla Cache's keys
-        (recurrent_state, conv_state, ffn_state). Kept for callers that still
-        want copies; the slot-native ops make this unnecessary."""
+    def gather_cache(self, slot_batch: Sequence[SlotDict], resident: bool | None = None):
+        """wkvm's RWKV7StateBank.gather_cache: an fla ``Cache`` seeded with the
+        batch's states (offset 0), for one model forward; commit it with
+        :meth:`scatter_cache`. wkvm's RWKV7Runner calls the pair around every
+        forward (wkvm/runner/runner.py:53-61, 79-87).
+
+        ``resident`` (default: whether ``fla_compat.install()`` is in effect)
+        picks what the cache holds. Resident: each layer's recurrent state is
+        a :class:`~wkvm_b200.fla_compat.SlotState` that the installed ops
+        update in place in ``wkv[layer, slot]``, and the token-shift rows are
+        gathered by one kernel; nothing of the wkv family is copied. Not
+        resident: plain tensor copies, as wkvm's bank gives them (one gather
+        kernel per family for all layers), for fla's own ops or any caller
+        that edits the states."""
+        from fla.models.utils import Cache
+
+        from . import fla_compat
+
         wkv_ids = _ids(slot_batch, "wkv")
         shift_ids = _ids(slot_batch, "shift")
-        out = []
+        if resident is None:
+            resident = fla_compat.installed()
+        if resident:
+            h = fla_compat.slot_cache(self, wkv_ids, shift_ids=shift_ids)
+            h.cache._wkvm_slot_handle = h
+            return h.cache
+        wkv = ops.slot_gather_outer_major(self.wkv, 1, wkv_ids)      # [L, n, H, K, V]
+        shift = ops.slot_gather_outer_major(self.shift, 2, shift_ids)  # [L, 2, n, D]
+        cache = Cache()
         for i in range(self.layout.n_layer):
-            out.append({
-                "recurrent_state": ops.slot_snapshot(self.wkv[i], 0, wkv_ids,
-                                                     out=self._dev_buf(self.wkv[i], len(wkv_ids))),
-                "conv_state": ops.slot_snapshot(self.shift[i, 0], 0, shift_ids,
-                                                out=self._dev_buf(self.shift[i, 0], len(shift_ids))),
-                "ffn_state": ops.slot_snapshot(self.shift[i, 1], 0, shift_ids,
-                                               out=self._dev_buf(self.shift[i, 1], len(shift_ids))),
-            })
-        return out
+            cache.update(recurrent_state=wkv[i], conv_state=shift[i, 0], ffn_state=shift[i, 1],
+                         layer_idx=i, offset=0)
+        return cache
 
     def scatter_cache(self, slot_batch: Sequence[SlotDict], cache) -> None:
+        """wkvm's RWKV7StateBank.scatter_cache: commits a forward's states
+        back to the batch's rows. For a resident cache only the token-shift
+        rows move (the wkv states were updated in place)."""
+        handle = getattr(cache, "_wkvm_slot_handle", None)
+        if handle is not None:
+            handle.commit()
+            return
         wkv_ids = _ids(slot_batch, "wkv")
         shift_ids = _ids(slot_batch, "shift")
         for i in range(self.layout.n_layer):
@@ -140,11 +163,6 @@ class RWKV7StateBank:
                              st["conv_state"].to(self.shift.dtype).contiguous())
             ops.slot_restore(self.shift[i, 1], 0, shift_ids,
                              st["ffn_state"].to(self.shift.dtype).contiguous())
-
-    @staticmethod
-    def _dev_buf(family_layer: torch.Tensor, n: int) -> torch.Tensor:
-        return torch.empty((n, *family_layer.shape[1:]), dtype=family_layer.dtype,
-                           device=family_layer.device)
 
     # -- snapshot / restore (wkvm/store.py:108-156) --------------------------
 

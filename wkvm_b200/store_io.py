@@ -138,15 +138,26 @@ def wake(bank, slots: Sequence[int], source) -> None:
     source = list(source)
     if len(source) != len(slots):
         raise ValueError("sessions and slots differ in length")
+    staged = []  # pinned copies of pageable sources, alive until the restores ran
     for s, t in zip(slots, source):
-        wkv, shift = _pinned_or_device(t["wkv"]), _pinned_or_device(t["shift"])
+        wkv = _pinned_or_device(t["wkv"], staged)
+        shift = _pinned_or_device(t["shift"], staged)
         ops.slot_restore(bank.wkv, 1, [s], wkv.reshape(1, *wkv.shape))
         ops.slot_restore(bank.shift, 2, [s], shift.reshape(1, *shift.shape))
+    if staged:
+        # the restore kernels read host memory directly, and torch's pinned
+        # allocator does not know it: a staged copy freed now could be handed
+        # out again while a restore still reads it
+        torch.cuda.current_stream(bank.device).synchronize()
 
 
-def _pinned_or_device(t: torch.Tensor) -> torch.Tensor:
+def _pinned_or_device(t: torch.Tensor, staged: list) -> torch.Tensor:
     t = t.contiguous()
-    return t if (t.is_cuda or t.is_pinned()) else t.pin_memory()
+    if t.is_cuda or t.is_pinned():
+        return t
+    p = t.pin_memory()
+    staged.append(p)
+    return p
 
 
 # ---------------------------------------------------------------- COLD tier
