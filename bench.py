@@ -45,6 +45,9 @@ import torch
 
 ROOT = Path(__file__).resolve().parent
 L, H, N, NUM_SLOTS, ACTIVE = 24, 32, 64, 1024, 256
+# N > 1 migration leg of the default run: 10 sessions every 4 steps (2.5 per
+# step, 1 % of the 256 active), drawn from PARKED live sessions
+MIG_EVERY, MIG_SLOTS, PARKED = 4, 10, 128
 BYTES_PER_HEAD = 2 * N * N * 4 + 6 * N * 2 + N * 2  # state r+w, 6 inputs, o = 33,664 B
 METRIC = "WKV-7 slot-decode tokens/s @1/2/4/8 B200; achieved HBM GB/s vs peak"
 PROFILE = ROOT / "profiles" / "wkv7_decode_slots_cfg1.txt"
@@ -193,8 +196,33 @@ def run_ours(args, world, rank, local):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         step()
-    for _ in range(args.warmup):
+    # N > 1: live migration around the ring, the path's only exchange. Every
+    # MIG_EVERY steps MIG_SLOTS parked sessions (live slots outside this
+    # step's decode batch) go to rank + 1 over one NCCL send/recv pair while
+    # rank - 1's arrive in newly allocated slots; a sent slot is freed only
+    # after the receiver's acknowledgement. All of it is stream-ordered on a
+    # side stream beside the decode graph; the host never waits.
+    mig = None
+    if world > 1 and not args.no_migration:
+        from wkvm_b200 import shard
+        arena = shard.ShardArena(NUM_SLOTS)
+        arena.claim(ids_host.tolist())
+        parked = arena.allocate(PARKED)
+        pack, unpack, empty = shard.bank_packer(bank)
+        mig = shard.RingMigrator(pack, unpack, empty, rank, world, device=dev, timeout=60.0)
+
+    def migrate(i):
+        if mig is None or i % MIG_EVERY:
+            return
+        arena.free(mig.reap())
+        out_ids, parked[:] = parked[:MIG_SLOTS], parked[MIG_SLOTS:]
+        in_ids = arena.allocate(MIG_SLOTS)
+        mig.start(out_ids, in_ids)
+        parked.extend(in_ids)
+
+    for i in range(args.warmup):
         graph.replay()
+        migrate(i)
     torch.cuda.synchronize(dev)
 
     barrier(world)
@@ -202,11 +230,16 @@ def run_ours(args, world, rank, local):
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(dev.index if dev.index is not None else 0) as clk:
         start.record()
-        for _ in range(args.steps):
+        for i in range(args.steps):
             graph.replay()
+            migrate(i)
+        if mig is not None:
+            torch.cuda.current_stream(dev).wait_stream(mig.stream)
         stop.record()
         torch.cuda.synchronize(dev)
     barrier(world)
+    if mig is not None:
+        arena.free(mig.reap(block=True))
     ms = max_over_ranks(start.elapsed_time(stop), world, dev)
     ops.check_device_status(dev)
 
@@ -263,6 +296,7 @@ def run_ours(args, world, rank, local):
         return None
     step_ms = ms / args.steps
     launch_ms = step_ms / L
+    per_slot_bytes = layout.wkv_bytes_per_slot() + layout.shift_bytes_per_slot()
     bytes_per_launch = ACTIVE * H * BYTES_PER_HEAD
     achieved = bytes_per_launch / (launch_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
@@ -286,10 +320,16 @@ def run_ours(args, world, rank, local):
                         "1024 arena slots per GPU, all layers per step",
             "global_batch": ACTIVE * world,
             "slots_per_gpu": NUM_SLOTS,
-            "parallelism": f"slot-sharded x{world}, no collective",
+            "parallelism": f"slot-sharded x{world}, no collective on the decode path"
+                           + ("" if mig is None else "; ring migration over NCCL send/recv"),
             "graph": f"CUDA graph of {L} per-layer launches"
                      + ("" if args.no_overlap else ", programmatic dependent launch between layers"),
             "l2": "no flush: 6.4 GB state traffic per step > 126 MB L2",
+            "migration": None if mig is None else (
+                f"{MIG_SLOTS} parked sessions ({MIG_SLOTS * per_slot_bytes} B) every {MIG_EVERY} "
+                "steps to rank+1 over one NCCL send/recv pair, restored on arrival, freed at "
+                "the source after the receiver's acknowledgement; side stream, inside the "
+                "timed region"),
         },
         "roofline": {
             "bound": "hbm",
@@ -303,7 +343,7 @@ def run_ours(args, world, rank, local):
             "traffic": traffic,
         },
         "clocks": clk.summary(),
-        "gpu_launches": L * args.steps,
+        "gpu_launches": L * args.steps + (0 if mig is None else 4 * ((args.steps + MIG_EVERY - 1) // MIG_EVERY)),
         "e2e": None if e2e_ms is None else {
             "value": round(world * ACTIVE * e_steps / (e2e_ms * 1e-3), 1),
             "unit": "tokens/s",
@@ -1063,6 +1103,8 @@ def main():
     ap.add_argument("--cpu-sample-slots", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-migration", action="store_true",
+                    help="N > 1: leave out the ring migration of parked sessions")
     ap.add_argument("--no-workloads", action="store_true",
                     help="skip the config 2 / 3 lines the default 1-GPU run adds")
     ap.add_argument("--no-overlap", action="store_true",

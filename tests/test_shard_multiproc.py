@@ -127,3 +127,49 @@ def test_shard_arena_and_map():
     src, dst = m.plan_move("a", 1 - g0.rank)
     m.commit_move("a", src, dst)
     assert m.where["a"] == dst and not m.arenas[src.rank].is_live(src.local)
+
+
+def _ring_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=20))
+    try:
+        bank = torch.zeros(9, 3, 5)
+        for s in range(1, 9):
+            bank[s] = 100 * rank + s + torch.arange(15.0).view(3, 5)
+        pack, unpack, empty = _cpu_packer(bank)
+        arena = shard.ShardArena(8)
+        live = arena.allocate(4)                       # slots 1..4 hold sessions
+        mig = shard.RingMigrator(pack, unpack, empty, rank, world, timeout=10)
+        incoming = arena.allocate(2)                   # step 1: destination allocates
+        mig.start([live[0], live[1]], incoming)        # steps 2-4
+        freed = mig.reap(block=True)                   # step 5: free after the ack
+        arena.free(freed)
+        src = (rank - 1) % world
+        expected = torch.stack([100 * src + s + torch.arange(15.0).view(3, 5) for s in (1, 2)])
+        q.put((rank, bool(torch.equal(bank[incoming], expected)), freed,
+               [arena.is_live(s) for s in (1, 2, 3, 4)], mig.in_flight))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_ring_migration_three_ranks():
+    """RingMigrator over three gloo ranks: every rank sends two sessions to
+    the next and receives two from the previous; the acknowledgement flows
+    back the other way and only then are the sent slots freed."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_ring_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    out = dict((item[0], item[1:]) for item in (q.get(timeout=60) for _ in range(3)))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(3):
+        ok, freed, live, in_flight = out[r]
+        assert ok, r
+        assert freed == [1, 2] and live == [False, False, True, True] and in_flight == 0

@@ -21,34 +21,6 @@ def _bank(cuda, fill=True):
     return b
 
 
-def test_gather_scatter_roundtrip(cuda):
-    bank = _bank(cuda, fill=False)
-    batch = [{"wkv": 2, "shift": 2}, {"wkv": 4, "shift": 4}]
-    cache = bank.gather_cache(batch)
-    for i in range(LAYOUT.n_layer):
-        for key in ("recurrent_state", "conv_state", "ffn_state"):
-            cache[i][key].normal_()
-    expected = [{k: v.clone() for k, v in c.items()} for c in cache]
-    bank.scatter_cache(batch, cache)
-    back = bank.gather_cache(batch)
-    for i in range(LAYOUT.n_layer):
-        for key in expected[i]:
-            assert torch.equal(back[i][key], expected[i][key])
-
-
-def test_scatter_leaves_other_slots_untouched(cuda):
-    bank = _bank(cuda, fill=False)
-    cache = bank.gather_cache([{"wkv": 3, "shift": 3}])
-    for i in range(LAYOUT.n_layer):
-        for key in cache[i]:
-            cache[i][key].fill_(1.0)
-    bank.scatter_cache([{"wkv": 3, "shift": 3}], cache)
-    for s in (0, 1, 2, 4):
-        assert bank.wkv[:, s].abs().sum().item() == 0.0
-        assert bank.shift[:, :, s].abs().sum().item() == 0.0
-    assert bank.wkv[:, 3].abs().sum().item() > 0.0
-
-
 def test_zero_slots(cuda):
     bank = _bank(cuda)
     before_w, before_s = bank.wkv.clone(), bank.shift.clone()

@@ -64,6 +64,15 @@ class ShardArena:
             self._live.remove(i)
             self._free.append(i)
 
+    def claim(self, ids: Sequence[int]) -> None:
+        """Marks the given free slots live (sessions placed by id)."""
+        for i in ids:
+            if i in self._live or not 0 < i <= self.num_slots:
+                raise KeyError(f"slot {i} is not free")
+        gone = set(ids)
+        self._free = [i for i in self._free if i not in gone]
+        self._live.update(gone)
+
     @property
     def num_free(self) -> int:
         return len(self._free)
@@ -191,3 +200,110 @@ def recv_slots(ids: Sequence[int], src_rank: int, unpack: Unpacker,
         torch.cuda.current_stream(buf.device).synchronize()
     ack = torch.full((1,), len(ids), dtype=torch.int32, device=buf.device)
     _wait(dist.isend(ack, src_rank, group=group, tag=tag + 1), timeout, "acknowledge")
+
+
+class RingMigrator:
+    """Migration around the ring rank -> rank + 1 that never blocks the host
+    (the steady-state form a serving loop uses between decode steps).
+
+    :meth:`start` enqueues, on a side stream that first waits for the
+    caller's current stream (so the outgoing rows are final): pack the
+    outgoing slots, one NCCL send to rank + 1 paired with one receive from
+    rank - 1, unpack into the caller's newly allocated slots, then the
+    acknowledgement exchange (each rank tells its sender how many slots it
+    restored). Nothing waits on the host. :meth:`fence` makes a stream wait
+    for the restores before it reads the incoming slots. :meth:`reap` returns
+    the outgoing slots whose acknowledgement has arrived, which the caller may
+    now free (step 5 of the protocol above); a migration unacknowledged for
+    ``timeout`` seconds raises MigrationTimeout and its slots stay allocated.
+
+    With CPU buffers (gloo) the same calls run synchronously."""
+
+    def __init__(self, pack: Packer, unpack: Unpacker, empty: Callable[[int], torch.Tensor],
+                 rank: int, world: int, *, device=None, group=None, timeout: float = 30.0):
+        if world < 2:
+            raise ValueError("migration needs at least two ranks")
+        self.pack, self.unpack, self.empty = pack, unpack, empty
+        self.rank, self.world, self.group, self.timeout = rank, world, group, timeout
+        self.dst, self.src = (rank + 1) % world, (rank - 1) % world
+        self.device = torch.device(device) if device is not None else None
+        cuda = self.device is not None and self.device.type == "cuda"
+        self.stream = torch.cuda.Stream(self.device) if cuda else None
+        self._pending: list = []
+        self._last = None
+
+    def _p2p(self, send: torch.Tensor, recv: torch.Tensor) -> None:
+        ops_ = [dist.P2POp(dist.isend, send, self.dst, group=self.group),
+                dist.P2POp(dist.irecv, recv, self.src, group=self.group)]
+        for w in dist.batch_isend_irecv(ops_):
+            w.wait()  # NCCL: the side stream waits; gloo: the host does
+
+    def start(self, out_ids: Sequence[int], in_ids: Sequence[int]) -> None:
+        """Sends ``out_ids`` to rank + 1 and receives rank - 1's slots into
+        ``in_ids`` (the same count on every rank)."""
+        import contextlib
+        import time
+
+        out_ids, in_ids = list(out_ids), list(in_ids)
+        if self.stream is not None:
+            self.stream.wait_stream(torch.cuda.current_stream(self.device))
+            ctx = torch.cuda.stream(self.stream)
+        else:
+            ctx = contextlib.nullcontext()
+        with ctx:
+            sendbuf = self.pack(out_ids)
+            recvbuf = self.empty(len(in_ids))
+            self._p2p(sendbuf, recvbuf)
+            self.unpack(in_ids, recvbuf)
+            dev = sendbuf.device
+            ack_out = torch.full((1,), len(in_ids), dtype=torch.int32, device=dev)
+            ack_in = torch.full((1,), -1, dtype=torch.int32, device=dev)
+            # the acknowledgement goes back to the sender (rank - 1) and ours
+            # comes from rank + 1: the ring in the other direction
+            ops_ = [dist.P2POp(dist.isend, ack_out, self.src, group=self.group),
+                    dist.P2POp(dist.irecv, ack_in, self.dst, group=self.group)]
+            for w in dist.batch_isend_irecv(ops_):
+                w.wait()
+            if self.stream is not None:
+                host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+                host.copy_(ack_in, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(self.stream)
+                for t in (sendbuf, recvbuf, ack_out, ack_in):
+                    t.record_stream(self.stream)
+            else:
+                host, ev = ack_in, None
+        self._last = ev
+        self._pending.append((ev, host, out_ids, time.monotonic()))
+
+    def fence(self, stream=None) -> None:
+        """Makes ``stream`` (default: current) wait for the restores so far."""
+        if self._last is not None:
+            (stream or torch.cuda.current_stream(self.device)).wait_event(self._last)
+
+    def reap(self, block: bool = False) -> list[int]:
+        """Outgoing slot ids acknowledged since the last call (free them)."""
+        import time
+
+        done, keep = [], []
+        for ev, host, ids, t0 in self._pending:
+            if ev is not None and not ev.query():
+                if block:
+                    while not ev.query():
+                        if time.monotonic() - t0 > self.timeout:
+                            raise MigrationTimeout("acknowledgement: timed out")
+                        time.sleep(1e-4)
+                elif time.monotonic() - t0 > self.timeout:
+                    raise MigrationTimeout(f"acknowledgement: none after {self.timeout}s")
+                else:
+                    keep.append((ev, host, ids, t0))
+                    continue
+            if int(host.item()) != len(ids):
+                raise RuntimeError(f"peer acknowledged {int(host.item())} of {len(ids)} slots")
+            done.extend(ids)
+        self._pending = keep
+        return done
+
+    @property
+    def in_flight(self) -> int:
+        return len(self._pending)
