@@ -54,6 +54,13 @@ enum {
 
 enum { WKVM_DTYPE_F32 = 0, WKVM_DTYPE_BF16 = 1, WKVM_DTYPE_F16 = 2 };
 
+/* OR-ed into the `dtype` argument of the gated-delta-rule entry points: the
+ * per-token gates g and beta are fp32 while q, k, v and o have the dtype in
+ * the low byte (fla's GDN layers commonly compute g in fp32; fla's kernels
+ * load every pointer in its own dtype). The 16-bit chunk paths then stay on
+ * the tensor cores. */
+#define WKVM_GATES_F32 0x100
+
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int wkvm_version(void);
 

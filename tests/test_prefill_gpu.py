@@ -217,3 +217,44 @@ def test_chunk_rwkv7_varlen_cu_seqlens(cuda):
     assert_out_close(o, ro)
     assert rel_err(ht, rh) < REL_TOL
     assert torch.equal(ht[1], d["h0"][1])
+
+
+@pytest.mark.parametrize("limit", [2 << 30, 0])  # two launches, one kernel
+def test_chunk_gdn_fp32_gates_stay_on_16bit_path(cuda, monkeypatch, limit):
+    """16-bit q/k/v with fp32 g and beta (what fla's GDN layers pass) runs the
+    16-bit chunk kernels: with gates that bf16 represents exactly the result
+    is bit-identical to the all-bf16 call (the recurrent fallback would round
+    differently), and gates that bf16 cannot hold match the oracle."""
+    monkeypatch.setattr(prefill, "GDN_WORKSPACE_LIMIT", limit)
+    B, T, H, K = 2, 200, 2, 128
+    x = synth.gdn_inputs(B, T, H, K, seed=12)
+    d = _to(x, cuda)
+    args = dict(scale=K ** -0.5, initial_state=d["h0"], output_final_state=True)
+    o16, h16 = ops.chunk_gated_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"], **args)
+    o32, h32 = ops.chunk_gated_delta_rule(d["q"], d["k"], d["v"], d["g"].float(),
+                                          d["beta"].float(), **args)
+    assert torch.equal(o16, o32) and torch.equal(h16, h32)
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, H, generator=torch.Generator().manual_seed(3)))
+    beta = torch.rand(B, T, H, generator=torch.Generator().manual_seed(4))
+    o, ht = ops.chunk_gated_delta_rule(d["q"], d["k"], d["v"], g.to(cuda), beta.to(cuda), **args)
+    ro, rh = oracle.gdn_recurrence(np32(x["q"]), np32(x["k"]), np32(x["v"]), g.numpy(),
+                                   beta.numpy(), initial_state=np32(x["h0"]))
+    ops.check_device_status(cuda)
+    assert o.dtype == torch.bfloat16
+    assert_out_close(o, ro)
+    assert rel_err(ht, rh) < REL_TOL
+
+
+def test_gdn_decode_fp32_gates(cuda):
+    B, H, K = 3, 2, 128
+    x = synth.gdn_inputs(B, 1, H, K, seed=13)
+    d = _to(x, cuda)
+    bank = torch.zeros(1, 5, H, K, K, device=cuda)
+    bank[0, [1, 2, 4]] = d["h0"]
+    o = ops.gdn_decode_slots(d["q"], d["k"], d["v"], d["g"].float(), d["beta"].float(), bank, 0,
+                             [1, 2, 4])
+    ro, rh = oracle.gdn_recurrence(*(np32(x[n]) for n in ("q", "k", "v", "g", "beta")),
+                                   initial_state=np32(x["h0"]))
+    assert o.dtype == torch.bfloat16
+    assert_out_close(o, ro)
+    assert rel_err(bank[0, [1, 2, 4]], rh) < REL_TOL

@@ -17,7 +17,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libwkvm_b200.so"
 SOURCES = ["recurrent.cu", "slots.cu", "selftest.cu", "chunk.cu", "gdn_chunk.cu", "gdn_wy.cu",
-           "gdn_static.cu", "timemix.cu", "shift_mix.cu"]
+           "gdn_static.cu", "timemix.cu", "shift_mix.cu", "tma.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

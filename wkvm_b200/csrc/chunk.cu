@@ -32,6 +32,7 @@
 // dplr_chunkwise in .../dplr/naive.py:41-101). tf32 operands keep the result
 // within 2e-3 of the fp32 recurrence after 4096 tokens; bf16 operands do not.
 #include "chunk_common.cuh"
+#include "tma.cuh"
 
 namespace wkvm {
 namespace {
@@ -47,11 +48,11 @@ constexpr uint32_t LBO_S = 144;    // S^T: padded so column writes hit distinct 
 constexpr uint32_t SBO_S = 16 * LBO_S;
 constexpr uint32_t KSTEP = 2 * LBO;  // 8 tf32 (32 bytes) of K per MMA
 constexpr int RS = 68;             // row stride (floats) of row-major scratch
-constexpr int STG_ROW = 144;       // bytes per staged 64 x 16-bit input row (+16 pad)
+constexpr uint32_t STG_TILE = CH * 128;  // one input stream's chunk: 64 rows x 128 B (TMA box)
 
 // shared-memory regions (bytes)
-constexpr uint32_t S_STG = 0;                                   // raw inputs [6][64 rows]
-constexpr uint32_t S_G = S_STG + NIN * CH * STG_ROW;            // G row-major (stride RS)
+constexpr uint32_t S_STG = 0;                                   // raw inputs [6][64 rows], swizzled
+constexpr uint32_t S_G = S_STG + NIN * STG_TILE;                // G row-major (stride RS)
 constexpr uint32_t S_AK = S_G + CH * RS * 4;                    // A_ak tile (row t, K = s)
 constexpr uint32_t S_AAB = S_AK + CH * RS * 4;                  // A_ab row-major
 constexpr uint32_t S_TT = S_AAB + CH * RS * 4;                  // (I - A_ab)^-1 tile (row t', K = t)
@@ -93,22 +94,23 @@ __device__ __forceinline__ void st4(float* p, const float* x) {
   *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
+// The six input streams of a chunk, one TMA box each (64 tokens x 64 x 16 bit).
+struct InMaps {
+  CUtensorMap m[NIN];
+};
 
+// Element k of row t of staged input stream `in` (128-byte swizzled tile).
 template <typename T>
 __device__ __forceinline__ float stg(const uint8_t* sm, int in, int t, int k) {
-  return to_f32(reinterpret_cast<const T*>(sm + S_STG + (in * CH + t) * STG_ROW)[k]);
+  return to_f32(*reinterpret_cast<const T*>(sm + S_STG + in * STG_TILE +
+                                            tma::sw128_off(t, (uint32_t)k * 2)));
 }
 
 // 8 consecutive 16-bit inputs of row t starting at column k (k % 8 == 0).
 template <typename T>
 __device__ __forceinline__ void stg8(const uint8_t* sm, int in, int t, int k, float (&x)[8]) {
-  const uint4 u = *reinterpret_cast<const uint4*>(sm + S_STG + (in * CH + t) * STG_ROW + k * 2);
+  const uint4 u = *reinterpret_cast<const uint4*>(sm + S_STG + in * STG_TILE +
+                                                  tma::sw128_off(t, (uint32_t)k * 2));
   const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
   for (int i = 0; i < 8; ++i) x[i] = to_f32(e[i]);
@@ -146,11 +148,13 @@ __device__ __forceinline__ float in_b(const uint8_t* sm, int t, int k) {
 // accumulator row is l = 32 (w & 3) + lane; rows 0..63 ("lo") carry the
 // a/k-side and state rows, rows 64..127 the r/b-side and output rows.
 template <typename Tin, bool MUL>
-__global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
+__global__ void __launch_bounds__(NTHREADS, 1)
+dplr_chunk_kernel(ChunkArgs p, const __grid_constant__ InMaps maps) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
   __shared__ uint64_t mbar;
+  __shared__ uint64_t tma_bar;  // input tiles of the next chunk landed
   __shared__ uint32_t tmem_slot;
   __shared__ float s_gc[HD];    // e^{G_C}
   __shared__ float s_ref[HD];   // G at the chunk midpoint
@@ -186,9 +190,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     bos = (int64_t)n * p.T;
     len = p.T;
   }
-  const char* gin[NIN] = {static_cast<const char*>(p.p0), static_cast<const char*>(p.p1),
-                          static_cast<const char*>(p.p2), static_cast<const char*>(p.p3),
-                          static_cast<const char*>(p.p4), static_cast<const char*>(p.p5)};
   Tin* __restrict__ go = static_cast<Tin*>(p.o);
   float* Grow = reinterpret_cast<float*>(sm + S_G);
   float* Aab = reinterpret_cast<float*>(sm + S_AAB);
@@ -197,7 +198,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     tc::tmem_alloc(&tmem_slot, TMEM_COLS);
     tc::tmem_relinquish();
   }
-  if (tid == 0) tc::mbar_init(&mbar, 1);
+  if (tid == 0) {
+    tc::mbar_init(&mbar, 1);
+    tc::mbar_init(&tma_bar, 1);
+    tc::fence_mbar_init();
+#pragma unroll
+    for (int i = 0; i < NIN; ++i) tma::prefetch_map(&maps.m[i]);
+  }
   // S^T[v][k] = h[k][v]; thread k = tid & 63 writes a quarter of column k
   for (int e = tid; e < HD * HD; e += NTHREADS) {
     const int k = e & 63, v = e >> 6;
@@ -222,29 +229,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
   const uint32_t idesc64 = tc::idesc_tf32(128, 64);
   const uint32_t idesc128 = tc::idesc_tf32(128, 128);
 
-  // Issues 16-byte async copies of chunk c's six 64 x 64 input tiles into the
-  // staging area (rows past the sequence end are zero-filled).
-  // Thread tid copies piece (tid & 7) of row t = (tid >> 3) & 63 of input
-  // streams (tid >> 9) + j, j stepping by NTHREADS / 512.
-  static_assert(NIN * CH * 8 % NTHREADS == 0, "staging map");
+  // Thread 0 issues the TMA loads of chunk c's six 64 x 64 input tiles (one
+  // box per stream, no multicast), counted on tma_bar. Rows past the end of
+  // the sequence are zeroed after they land (see the loop head).
+  uint32_t tphase = 0;
+  bool tma_pending = false;
   auto stage = [&](int c) {
-    const int64_t t0 = bos + (int64_t)c * CH;
-    const int64_t rem = len - (int64_t)c * CH;
-    const int cl = rem < CH ? (int)rem : CH;
-    const uint32_t base = tc::smem_u32(sm + S_STG);
-    const int piece = tid & 7;
-    const int64_t gstride = (int64_t)H * HD * 2;  // bytes between tokens
-    const int64_t goff = (t0 * H + hh) * HD * 2 + piece * 16;
+    if (tid == 0) {
+      tc::mbar_expect_tx(&tma_bar, NIN * STG_TILE);
+      const int tok = (int)(bos + (int64_t)c * CH);
 #pragma unroll
-    for (int j = 0; j < NIN * CH * 8 / NTHREADS; ++j) {
-      const int e = tid + NTHREADS * j;
-      const int in = e >> 9;
-      const int t = (e >> 3) & 63;
-      const uint32_t off = (in * CH + t) * STG_ROW + piece * 16;
-      if (t < cl) cp_async16(base + off, gin[in] + goff + t * gstride);
-      else *reinterpret_cast<uint4*>(sm + S_STG + off) = make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < NIN; ++i)
+        tma::load_rows(sm + S_STG + i * STG_TILE, &maps.m[i], hh, tok, &tma_bar);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    tma_pending = true;
   };
   if (nchunks > 0) stage(0);
 
@@ -255,9 +253,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     const bool last = (c == nchunks - 1);
 
     // ---- the chunk's raw inputs were staged by the previous iteration (or
-    //      before the loop); wait for the async copies to land
-    cp_async_wait_all();
-    __syncthreads();
+    //      before the loop); wait for the TMA loads to land (warp 0 polls)
+    {
+      const bool ok = warp != 0 || tc::mbar_wait(&tma_bar, tphase);
+      if (__syncthreads_or(!ok)) {  // the loads stay pending: waited for once more below
+        if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+        failed = true;
+        break;
+      }
+      tphase ^= 1u;
+      tma_pending = false;
+      if (clen < CH) {  // rows past the sequence end hold the next one's tokens
+        for (int e = tid; e < NIN * (CH - clen) * 8; e += NTHREADS) {
+          const int in = e / ((CH - clen) * 8), rest = e - in * (CH - clen) * 8;
+          *reinterpret_cast<uint4*>(sm + S_STG + in * STG_TILE + (clen + (rest >> 3)) * 128 +
+                                    (rest & 7) * 16) = make_uint4(0, 0, 0, 0);
+        }
+        __syncthreads();
+      }
+    }
 
     // ---- E1: inclusive scan of w down each column by all threads: thread
     //      (column k = tid & 63, segment tid >> 6) scans 8 tokens, then adds
@@ -563,7 +577,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
     sync_tc();
   }
 
-  cp_async_wait_all();  // no copy may still target this CTA's shared memory
+  // no TMA load may still target this CTA's shared memory
+  if (tma_pending && !(warp != 0 || tc::mbar_wait(&tma_bar, tphase)) && tid == 0)
+    report(p.status, WKVM_ERR_TIMEOUT);
+  __syncthreads();
   if (failed) {
     // an MMA group may still be running: give it a bounded chance to land
     tc::mbar_wait(&mbar, phase ^ 1u);
@@ -575,11 +592,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) dplr_chunk_kernel(ChunkArgs p) {
   if (warp == 0) tc::tmem_dealloc(tm, TMEM_COLS);
 }
 
+// `tokens`: rows of the activation tensors (B * T, or the varlen total T).
 template <typename Tin, bool MUL>
-int launch_chunk_t(const ChunkArgs& a, int nblocks, cudaStream_t stream) {
+int launch_chunk_t(const ChunkArgs& a, int nblocks, int64_t tokens, cudaStream_t stream) {
   auto k = dplr_chunk_kernel<Tin, MUL>;
+  InMaps maps;
+  const void* in[NIN] = {a.p0, a.p1, a.p2, a.p3, a.p4, a.p5};
+  for (int i = 0; i < NIN; ++i) {
+    const int rc = tma::encode_rows(&maps.m[i], in[i], tokens, a.H, HD, CH);
+    if (rc != WKVM_OK) return rc;
+  }
   WKVM_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-  k<<<nblocks, NTHREADS, SMEM_BYTES, stream>>>(a);
+  k<<<nblocks, NTHREADS, SMEM_BYTES, stream>>>(a, maps);
   return cudaGetLastError() == cudaSuccess ? WKVM_OK : WKVM_ERR_CUDA;
 }
 
@@ -625,11 +649,14 @@ extern "C" int wkvm_chunk_dplr(const void* r, const void* w, const void* k, cons
   if (B < 0 || T < 0 || H <= 0) return WKVM_ERR_INVALID_ARG;
   if (B == 0) return WKVM_OK;
   if (!r || !w || !k || !v || !a || !b || !o) return WKVM_ERR_INVALID_ARG;
+  const int64_t tokens = cu_seqlens ? (int64_t)T : (int64_t)B * T;
+  if (tokens == 0) return wkvm_fused_recurrent_dplr(r, w, k, v, a, b, o, h0, ht, cu_seqlens, B, T,
+                                                    H, K, V, scale, dtype, status, stream);
   if ((h0 && !wkvm::al16(h0)) || (ht && !wkvm::al16(ht))) return WKVM_ERR_ALIGN;
   wkvm::ChunkArgs args{r, w, k, v, a, b, o, h0, ht, nullptr, 0, cu_seqlens, T, H, scale, status};
   if (dtype == WKVM_DTYPE_BF16)
-    return wkvm::launch_chunk_t<__nv_bfloat16, false>(args, B * H, (cudaStream_t)stream);
-  return wkvm::launch_chunk_t<__half, false>(args, B * H, (cudaStream_t)stream);
+    return wkvm::launch_chunk_t<__nv_bfloat16, false>(args, B * H, tokens, (cudaStream_t)stream);
+  return wkvm::launch_chunk_t<__half, false>(args, B * H, tokens, (cudaStream_t)stream);
 }
 
 extern "C" int wkvm_wkv7_prefill_slots(const void* r, const void* w, const void* k, const void* v,
@@ -648,11 +675,13 @@ extern "C" int wkvm_wkv7_prefill_slots(const void* r, const void* w, const void*
   if (B < 0 || T < 0 || H <= 0) return WKVM_ERR_INVALID_ARG;
   if (B == 0) return WKVM_OK;
   if (!wkvm::al16(bank_layer)) return WKVM_ERR_ALIGN;
+  const int64_t tokens = cu_seqlens ? (int64_t)T : (int64_t)B * T;
+  if (tokens == 0) return WKVM_OK;  // the slots keep their state
   wkvm::ChunkArgs args{r, w, k, v, kk, a, o, bank_layer, bank_layer, slot_ids, num_slots,
                        cu_seqlens, T, H, 1.0f, status};
   if (dtype == WKVM_DTYPE_BF16)
-    return wkvm::launch_chunk_t<__nv_bfloat16, true>(args, B * H, (cudaStream_t)stream);
-  return wkvm::launch_chunk_t<__half, true>(args, B * H, (cudaStream_t)stream);
+    return wkvm::launch_chunk_t<__nv_bfloat16, true>(args, B * H, tokens, (cudaStream_t)stream);
+  return wkvm::launch_chunk_t<__half, true>(args, B * H, tokens, (cudaStream_t)stream);
 }
 
 extern "C" int wkvm_dplr_prefill_slots(const void* r, const void* w, const void* k, const void* v,
@@ -667,9 +696,11 @@ extern "C" int wkvm_dplr_prefill_slots(const void* r, const void* w, const void*
   if (B < 0 || T < 0 || H <= 0) return WKVM_ERR_INVALID_ARG;
   if (B == 0) return WKVM_OK;
   if (!wkvm::al16(bank_layer)) return WKVM_ERR_ALIGN;
+  const int64_t tokens = cu_seqlens ? (int64_t)T : (int64_t)B * T;
+  if (tokens == 0) return WKVM_OK;  // the slots keep their state
   wkvm::ChunkArgs args{r, w, k, v, a, b, o, bank_layer, bank_layer, slot_ids, num_slots,
                        cu_seqlens, T, H, scale, status};
   if (dtype == WKVM_DTYPE_BF16)
-    return wkvm::launch_chunk_t<__nv_bfloat16, false>(args, B * H, (cudaStream_t)stream);
-  return wkvm::launch_chunk_t<__half, false>(args, B * H, (cudaStream_t)stream);
+    return wkvm::launch_chunk_t<__nv_bfloat16, false>(args, B * H, tokens, (cudaStream_t)stream);
+  return wkvm::launch_chunk_t<__half, false>(args, B * H, tokens, (cudaStream_t)stream);
 }

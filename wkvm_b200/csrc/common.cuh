@@ -25,6 +25,13 @@ template <> __device__ __forceinline__ float from_f32<float>(float x) { return x
 template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
 
+// A per-token gate (g or beta) of the gated delta rule: fp32 when the caller
+// passed WKVM_GATES_F32, else the activation dtype.
+template <typename Tin>
+__device__ __forceinline__ float load_gate(const void* p, int64_t i, bool f32) {
+  return f32 ? static_cast<const float*>(p)[i] : to_f32(static_cast<const Tin*>(p)[i]);
+}
+
 // Streaming 128-bit state access. The recurrent state of one (slot, head) is
 // touched exactly once per kernel launch, so loads bypass L1 allocation and
 // stores skip L1 too: nothing in the launch re-reads them. The state is

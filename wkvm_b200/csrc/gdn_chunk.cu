@@ -81,6 +81,7 @@ struct GdnArgs {
   float scale;
   bool l2norm;
   int* status;
+  bool gates_f32 = false;  // g and beta are fp32 (WKVM_GATES_F32)
 };
 
 template <typename T>
@@ -142,8 +143,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_chunk_kernel(GdnArgs p) {
   const Tin* __restrict__ gq = static_cast<const Tin*>(p.q);
   const Tin* __restrict__ gk = static_cast<const Tin*>(p.k);
   const Tin* __restrict__ gv = static_cast<const Tin*>(p.v);
-  const Tin* __restrict__ gg = static_cast<const Tin*>(p.g);
-  const Tin* __restrict__ gb = static_cast<const Tin*>(p.beta);
   Tin* __restrict__ go = static_cast<Tin*>(p.o);
 
   if (warp == 0) {
@@ -221,8 +220,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) gdn_chunk_kernel(GdnArgs p) {
       const int t = tid;
       const bool valid = t < clen;
       const int64_t gi = (tok0 + t) * HV + hv;
-      const float gt = valid ? to_f32(gg[gi]) : 0.f;
-      const float bt = valid ? to_f32(gb[gi]) : 0.f;
+      const float gt = valid ? load_gate<Tin>(p.g, gi, p.gates_f32) : 0.f;
+      const float bt = valid ? load_gate<Tin>(p.beta, gi, p.gates_f32) : 0.f;
       float kn = 1.f, qn = 1.f;
       if (p.l2norm) {
         float sk = 0.f, sq = 0.f;
@@ -540,13 +539,16 @@ bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
 
 bool gdn_chunk_ok(int K, int V, int dtype, const void* q, const void* k, const void* v,
                   const void* o) {
-  return K == KD && V == VD && (dtype == WKVM_DTYPE_BF16 || dtype == WKVM_DTYPE_F16) &&
+  const int act = dtype & ~WKVM_GATES_F32;
+  return K == KD && V == VD && (act == WKVM_DTYPE_BF16 || act == WKVM_DTYPE_F16) &&
          al16(q) && al16(k) && al16(v) && al16(o);
 }
 
-int run_gdn_chunk(const GdnArgs& a, int nseq, int dtype, cudaStream_t stream) {
+int run_gdn_chunk(GdnArgs a, int nseq, int dtype, cudaStream_t stream) {
   const int nblocks = nseq * a.HV * 2;
-  if (dtype == WKVM_DTYPE_BF16) return launch_gdn_chunk<__nv_bfloat16>(a, nblocks, stream);
+  a.gates_f32 = (dtype & WKVM_GATES_F32) != 0;
+  if ((dtype & ~WKVM_GATES_F32) == WKVM_DTYPE_BF16)
+    return launch_gdn_chunk<__nv_bfloat16>(a, nblocks, stream);
   return launch_gdn_chunk<__half>(a, nblocks, stream);
 }
 

@@ -93,7 +93,8 @@ extern "C" int wkvm_chunk_gated_delta_rule_static(
     int32_t HV, int32_t K, int32_t V, float scale, int32_t use_qk_l2norm, int32_t dtype,
     int32_t* status, wkvm_stream_t stream) {
   if (K != 128 || V != 128) return WKVM_ERR_SHAPE;
-  if (dtype != WKVM_DTYPE_BF16 && dtype != WKVM_DTYPE_F16) return WKVM_ERR_DTYPE;
+  const int act = dtype & ~WKVM_GATES_F32;
+  if (act != WKVM_DTYPE_BF16 && act != WKVM_DTYPE_F16) return WKVM_ERR_DTYPE;
   if (B < 0 || T < 0 || H <= 0 || HV <= 0 || HV % H) return WKVM_ERR_INVALID_ARG;
   if (B == 0) return WKVM_OK;
   if (!q || !k || !v || !g || !beta || !o) return WKVM_ERR_INVALID_ARG;

@@ -63,6 +63,7 @@ struct WyArgs {
   float scale;
   bool l2norm;
   int* status;
+  bool gates_f32;  // g and beta are fp32 (WKVM_GATES_F32)
 };
 
 struct StateArgs {
@@ -163,8 +164,6 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
   const Tin* __restrict__ gq = static_cast<const Tin*>(p.q);
   const Tin* __restrict__ gk = static_cast<const Tin*>(p.k);
   const Tin* __restrict__ gv = static_cast<const Tin*>(p.v);
-  const Tin* __restrict__ gg = static_cast<const Tin*>(p.g);
-  const Tin* __restrict__ gb = static_cast<const Tin*>(p.beta);
   constexpr bool kBf16 = std::is_same<Tin, __nv_bfloat16>::value;
 
   if (warp == 0) {
@@ -201,12 +200,12 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
     x[0] = x[1] = x[2] = x[3] = 0.f;
     if (warp == 0) {
       if (lane < J.clen) {
-        x[0] = to_f32(gg[(J.tok0 + lane) * HV + J.hv]);
-        x[2] = to_f32(gb[(J.tok0 + lane) * HV + J.hv]);
+        x[0] = load_gate<Tin>(p.g, (J.tok0 + lane) * HV + J.hv, p.gates_f32);
+        x[2] = load_gate<Tin>(p.beta, (J.tok0 + lane) * HV + J.hv, p.gates_f32);
       }
       if (lane + 32 < J.clen) {
-        x[1] = to_f32(gg[(J.tok0 + lane + 32) * HV + J.hv]);
-        x[3] = to_f32(gb[(J.tok0 + lane + 32) * HV + J.hv]);
+        x[1] = load_gate<Tin>(p.g, (J.tok0 + lane + 32) * HV + J.hv, p.gates_f32);
+        x[3] = load_gate<Tin>(p.beta, (J.tok0 + lane + 32) * HV + J.hv, p.gates_f32);
       }
     }
   };
@@ -758,8 +757,9 @@ int gdn_two_phase(const void* q, const void* k, const void* v, const void* g, co
   if (W * nseq * HV > 0x7fffffff) W = 0x7fffffff / ((int64_t)nseq * HV);
   if (W < 1) return WKVM_ERR_UNSUPPORTED;
   if (nseq > 65535 || HV > 65535) return WKVM_ERR_UNSUPPORTED;
-  WyArgs wa{q, k, v, g, beta, recs, cu, T, H, HV, 0, (int)W, nseq, scale, l2norm, status};
-  return dtype == WKVM_DTYPE_BF16
+  WyArgs wa{q, k, v, g, beta, recs, cu, T, H, HV, 0, (int)W, nseq, scale, l2norm, status,
+            (dtype & WKVM_GATES_F32) != 0};
+  return (dtype & ~WKVM_GATES_F32) == WKVM_DTYPE_BF16
              ? run_windows<__nv_bfloat16>(wa, ids, num_slots, h_in, h_out, slots, carry, o, nseq,
                                          max_chunks, W, stream)
              : run_windows<__half>(wa, ids, num_slots, h_in, h_out, slots, carry, o, nseq,

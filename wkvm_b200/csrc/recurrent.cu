@@ -234,11 +234,11 @@ wkv7_recurrent_kernel(const Tin* __restrict__ r, const Tin* __restrict__ w,
 template <int K, int V, int ROWS, typename Tin>
 __global__ void __launch_bounds__((V / 4) * (K / ROWS))
 gdn_recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
-                     const Tin* __restrict__ v, const Tin* __restrict__ g,
-                     const Tin* __restrict__ beta, Tin* __restrict__ o,
+                     const Tin* __restrict__ v, const void* __restrict__ g,
+                     const void* __restrict__ beta, Tin* __restrict__ o,
                      const float* h_in, float* h_out, const int32_t* __restrict__ ids,
                      int64_t num_slots, const int64_t* __restrict__ cu_seqlens, int T, int H,
-                     int HV, float scale, bool l2norm, int* status) {
+                     int HV, float scale, bool l2norm, bool gates_f32, int* status) {
   constexpr int CG = V / 4;
   constexpr int RG = K / ROWS;
   constexpr int NT = CG * RG;
@@ -276,7 +276,8 @@ gdn_recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
   }
 
   // Inputs of token t+1 are fetched into registers while token t computes.
-  Tin nq = Tin(), nk = Tin(), nv = Tin(), ng = Tin(), nb = Tin();
+  Tin nq = Tin(), nk = Tin(), nv = Tin();
+  float ng = 0.f, nb = 0.f;
   auto fetch = [&](int64_t t) {
     const int64_t tk = sr.bos + t;
     if (tid < K) {
@@ -284,8 +285,8 @@ gdn_recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
       nk = k[(tk * H + hq) * (int64_t)K + tid];
     }
     if (tid < V) nv = v[(tk * HV + hv) * (int64_t)V + tid];
-    ng = g[tk * HV + hv];
-    nb = beta[tk * HV + hv];
+    ng = load_gate<Tin>(g, tk * HV + hv, gates_f32);
+    nb = load_gate<Tin>(beta, tk * HV + hv, gates_f32);
   };
   if (sr.len > 0) fetch(0);
 
@@ -294,8 +295,8 @@ gdn_recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
     const int64_t tok = sr.bos + t;
     const int64_t v_base = (tok * HV + hv) * (int64_t)V;
     const float cur_v = to_f32(nv);
-    const float cur_g = to_f32(ng);
-    const float cur_b = to_f32(nb);
+    const float cur_g = ng;
+    const float cur_b = nb;
     const float qq = to_f32(nq);
     const float kv = to_f32(nk);
     if (t + 1 < sr.len) fetch(t + 1);
@@ -396,7 +397,8 @@ struct RecArgs {
   bool l2norm;
   int* status;
   cudaStream_t stream;
-  bool overlap = false;  // programmatic dependent launch (decode only)
+  bool overlap = false;    // programmatic dependent launch (decode only)
+  bool gates_f32 = false;  // GDN: g and beta are fp32 (WKVM_GATES_F32)
 };
 
 // Process-wide opt-in for overlapping consecutive decode launches.
@@ -454,9 +456,9 @@ int launch_gdn_t(const RecArgs& a) {
   constexpr int NT = (V / 4) * (K / ROWS);
   dim3 grid((unsigned)((int64_t)a.B * a.HV));
   gdn_recurrent_kernel<K, V, ROWS, Tin><<<grid, NT, 0, a.stream>>>(
-      (const Tin*)a.p0, (const Tin*)a.p1, (const Tin*)a.p2, (const Tin*)a.p3,
-      (const Tin*)a.p4, (Tin*)a.o, a.h_in, a.h_out, a.ids, a.num_slots, a.cu, a.T, a.H, a.HV,
-      a.scale, a.l2norm, a.status);
+      (const Tin*)a.p0, (const Tin*)a.p1, (const Tin*)a.p2, a.p3, a.p4, (Tin*)a.o, a.h_in,
+      a.h_out, a.ids, a.num_slots, a.cu, a.T, a.H, a.HV, a.scale, a.l2norm, a.gates_f32,
+      a.status);
   return cudaGetLastError() == cudaSuccess ? WKVM_OK : WKVM_ERR_CUDA;
 }
 
@@ -467,8 +469,9 @@ int launch_gdn_kv(const RecArgs& a) {
   return WKVM_ERR_SHAPE;
 }
 
-int launch_gdn(const RecArgs& a, int dtype) {
-  switch (dtype) {
+int launch_gdn(RecArgs a, int dtype) {
+  a.gates_f32 = (dtype & WKVM_GATES_F32) != 0;
+  switch (dtype & ~WKVM_GATES_F32) {
     case WKVM_DTYPE_F32: return launch_gdn_kv<float>(a);
     case WKVM_DTYPE_BF16: return launch_gdn_kv<__nv_bfloat16>(a);
     case WKVM_DTYPE_F16: return launch_gdn_kv<__half>(a);

@@ -111,6 +111,23 @@ def _acts(*ts):
     return tuple(t.contiguous() for t in ts), _DTYPES[dt]
 
 
+GATES_F32 = 0x100  # WKVM_GATES_F32: g and beta fp32, q/k/v/o in the low byte's dtype
+
+
+def _gdn_acts(q, k, v, g, beta):
+    """Activations of the gated delta rule. q, k, v sharing a dtype keep it;
+    gates of another dtype are widened to fp32 (lossless) and flagged, so a
+    16-bit q/k/v with fp32 g/beta (what fla's GDN layers pass) stays on the
+    16-bit paths. q, k, v of mixed dtypes are all promoted to fp32."""
+    dt = q.dtype
+    if k.dtype != dt or v.dtype != dt or dt not in _DTYPES:
+        return _acts(q, k, v, g, beta)
+    if g.dtype == dt and beta.dtype == dt:
+        return tuple(t.contiguous() for t in (q, k, v, g, beta)), _DTYPES[dt]
+    gates = tuple(t.to(torch.float32).contiguous() for t in (g, beta))
+    return (q.contiguous(), k.contiguous(), v.contiguous(), *gates), _DTYPES[dt] | GATES_F32
+
+
 def _state(t: torch.Tensor | None) -> torch.Tensor | None:
     if t is None:
         return None
@@ -247,7 +264,7 @@ def fused_recurrent_gated_delta_rule(q, k, v, g=None, gk=None, gv=None, beta=Non
     if scale is None:
         scale = k.shape[-1] ** -0.5
     _require_cuda(q, k, v, g, beta, initial_state)
-    (q, k, v, g, beta), dt = _acts(q, k, v, g, beta)
+    (q, k, v, g, beta), dt = _gdn_acts(q, k, v, g, beta)
     B, T, H, K = q.shape
     HV, V = v.shape[2], v.shape[3]
     N = B if cu_seqlens is None else len(cu_seqlens) - 1
@@ -363,7 +380,7 @@ def gdn_decode_slots(q, k, v, g, beta, bank: torch.Tensor, layer: int, slot_ids,
     ([L, S+1, HV, K, V] fp32, in place). Returns o [B, T, HV, V]."""
     _require_cuda(q, k, v, g, beta, bank)
     layer_t = _bank_layer(bank, layer)
-    (q, k, v, g, beta), dt = _acts(q, k, v, g, beta)
+    (q, k, v, g, beta), dt = _gdn_acts(q, k, v, g, beta)
     B, T, H, K = q.shape
     HV, V = v.shape[2], v.shape[3]
     if tuple(layer_t.shape[1:]) != (HV, K, V):

@@ -49,7 +49,7 @@ def chunk_gdn(q, k, v, g, beta, scale, initial_state, output_final_state, use_qk
               cu_seqlens):
     """fla chunk_gated_delta_rule semantics; returns (o, final_state or None)."""
     _ops._require_cuda(q, k, v, g, beta, initial_state)
-    (q, k, v, g, beta), dt = _ops._acts(q, k, v, g, beta)
+    (q, k, v, g, beta), dt = _ops._gdn_acts(q, k, v, g, beta)
     B, T, H, K = q.shape
     HV, V = v.shape[2], v.shape[3]
     N = B if cu_seqlens is None else len(cu_seqlens) - 1
@@ -98,7 +98,7 @@ def gdn_prefill_slots(q, k, v, g, beta, bank, layer, slot_ids, scale, use_qk_l2n
     """Chunked GDN prefill with initial and final state in bank[layer, slot_ids]."""
     _ops._require_cuda(q, k, v, g, beta, bank)
     layer_t = _ops._bank_layer(bank, layer)
-    (q, k, v, g, beta), dt = _ops._acts(q, k, v, g, beta)
+    (q, k, v, g, beta), dt = _ops._gdn_acts(q, k, v, g, beta)
     B, T, H, K = q.shape
     HV, V = v.shape[2], v.shape[3]
     if tuple(layer_t.shape[1:]) != (HV, K, V):
