@@ -27,6 +27,7 @@
 #include <type_traits>
 
 #include "chunk_common.cuh"
+#include "tma.cuh"
 
 namespace wkvm {
 
@@ -96,15 +97,16 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 constexpr int WY_THREADS = 256;
 // Persistent: each CTA works through jobs (chunk, sequence, value head) with a
 // two-stage pipeline; job j+1's inputs land while job j computes.
-// A stage: [k; q] rows as a 16-bit K-major tile (128 rows x K = 128, SBO 2048;
-// the operands of the Gram MMA, copied in place by cp.async) and the v rows
-// (16-bit, row-major, padded). Once the stage's k and v have been read,
-// its first bytes hold -A (row-major), the inverse's scratch and the T tile.
-constexpr uint32_t SBO_H = 2048;                      // 16-bit tile, K = 128
-constexpr uint32_t V_ROW = VD * 2 + 16;
-constexpr uint32_t ST_QK = 0;
-constexpr uint32_t ST_V = ST_QK + 2 * CH * KD * 2;    // 32 KiB
-constexpr uint32_t STAGE = ST_V + CH * V_ROW;         // 50176 B
+// A stage holds one job's rows as TMA wrote them (six boxes of 64 tokens x
+// 64 elements, 128-byte swizzle): the [k; q] tile in two column blocks of
+// 128 rows x 128 bytes (block b: columns 64b..64b+63; rows 0..63 k, 64..127
+// q) -- directly the K-major operands of the Gram MMA -- then v in two
+// column blocks of 64 rows. Once the stage's k and v have been read, its
+// first bytes hold -A (row-major), the inverse's scratch and the T tile.
+constexpr uint32_t BOX = CH * 128;                    // one TMA box, 8 KiB
+constexpr uint32_t ST_QK = 0;                         // 2 blocks x 16 KiB
+constexpr uint32_t ST_V = ST_QK + 4 * BOX;            // 2 blocks x 8 KiB
+constexpr uint32_t STAGE = ST_V + 2 * BOX;            // 48 KiB
 constexpr uint32_t WS_AAB = 0;                        // within the job's stage
 constexpr uint32_t WS_TR = WS_AAB + CH * RS * 4;
 constexpr uint32_t WS_TT = WS_AAB;                    // written after -A is spent
@@ -116,10 +118,19 @@ static_assert(CH * W_ROW * 4 <= STAGE, "W staging outside the stage");
 constexpr uint32_t WY_TMEM_COLS = 256;
 constexpr uint32_t T_D1 = 0, T_AV = 64, T_AK = 128, T_DW = 192;
 
-// Byte offset of element (row, k) of a 16-bit K-major tile with SBO 2048.
-__device__ __forceinline__ uint32_t hoff(int row, int k) {
-  return (row >> 3) * SBO_H + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2;
+// Byte offsets within a stage of element (row, col) of the [k; q] tile
+// (rows 0..127) and of the v rows (0..63); col % 8 == 0 for 16-byte reads.
+__device__ __forceinline__ uint32_t qk_off(int row, int col) {
+  return ST_QK + (uint32_t)(col >> 6) * 2 * BOX + tma::sw128_off(row, (uint32_t)(col & 63) * 2);
 }
+__device__ __forceinline__ uint32_t v_off(int row, int col) {
+  return ST_V + (uint32_t)(col >> 6) * BOX + tma::sw128_off(row, (uint32_t)(col & 63) * 2);
+}
+
+// TMA descriptions of q, k ([tokens, H, 128]) and v ([tokens, HV, 128]).
+struct WyMaps {
+  CUtensorMap q, k, v;
+};
 
 struct Job {
   int n, hv, cw;   // sequence, value head, chunk within the window
@@ -148,10 +159,12 @@ __device__ __forceinline__ Job job_of(const WyArgs& p, int j) {
 }
 
 template <typename Tin>
-__global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njobs) {
+__global__ void __launch_bounds__(WY_THREADS, 2)
+gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   __shared__ uint64_t mbar;
+  __shared__ uint64_t in_bar[2];  // a stage's TMA loads landed
   __shared__ uint32_t tmem_slot;
   __shared__ float s_beta[CH], s_G[CH], s_eG[CH], s_eGC[CH], s_rk[CH], s_rq[CH];
 
@@ -161,39 +174,39 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
   const bool lo = l < 64;
   const int r64 = l & 63;
   const int H = p.H, HV = p.HV;
-  const Tin* __restrict__ gq = static_cast<const Tin*>(p.q);
-  const Tin* __restrict__ gk = static_cast<const Tin*>(p.k);
-  const Tin* __restrict__ gv = static_cast<const Tin*>(p.v);
   constexpr bool kBf16 = std::is_same<Tin, __nv_bfloat16>::value;
 
   if (warp == 0) {
     tc::tmem_alloc(&tmem_slot, WY_TMEM_COLS);
     tc::tmem_relinquish();
   }
-  if (tid == 0) tc::mbar_init(&mbar, 1);
+  if (tid == 0) {
+    tc::mbar_init(&mbar, 1);
+    tc::mbar_init(&in_bar[0], 1);
+    tc::mbar_init(&in_bar[1], 1);
+    tc::fence_mbar_init();
+    tma::prefetch_map(&maps.q);
+    tma::prefetch_map(&maps.k);
+    tma::prefetch_map(&maps.v);
+  }
 
-  // async copies of job J's q, k, v rows into stage st (zeros past clen);
-  // every thread commits one group per call, empty or not
+  // TMA loads of job J's k, q, v rows into stage st (thread 0; nothing for a
+  // job past its sequence's end). Rows past clen are zeroed once they land.
+  uint32_t in_phase = 0u, in_pending = 0u;  // bit st: stage st's parity / a load in flight
   auto stage_in = [&](const Job& J, int st) {
-    const uint32_t base = tc::smem_u32(sm + st * STAGE);
+    if (J.clen <= 0) return;
+    in_pending |= 1u << st;
+    if (tid != 0) return;
+    uint8_t* base = sm + st * STAGE;
     const int hq = J.hv / (HV / H);
+    const int tok = (int)J.tok0;
+    tc::mbar_expect_tx(&in_bar[st], 6 * BOX);
 #pragma unroll
-    for (int j = 0; j < 3 * CH * 16 / WY_THREADS; ++j) {
-      const int e = tid + WY_THREADS * j;
-      const int which = e >> 10, t = (e >> 4) & 63, piece = e & 15;  // 0 k, 1 q, 2 v
-      uint32_t off;
-      const Tin* src;
-      if (which < 2) {
-        off = ST_QK + hoff(which * 64 + t, piece * 8);
-        src = (which ? gq : gk) + ((J.tok0 + t) * H + hq) * KD + piece * 8;
-      } else {
-        off = ST_V + t * V_ROW + piece * 16;
-        src = gv + ((J.tok0 + t) * HV + J.hv) * VD + piece * 8;
-      }
-      if (t < J.clen) chunkc::cp_async16(base + off, src);
-      else *reinterpret_cast<uint4*>(sm + st * STAGE + off) = make_uint4(0, 0, 0, 0);
+    for (int b = 0; b < 2; ++b) {
+      tma::load_rows(base + ST_QK + b * 2 * BOX, &maps.k, hq, tok, &in_bar[st], 64 * b);
+      tma::load_rows(base + ST_QK + b * 2 * BOX + BOX, &maps.q, hq, tok, &in_bar[st], 64 * b);
+      tma::load_rows(base + ST_V + b * BOX, &maps.v, J.hv, tok, &in_bar[st], 64 * b);
     }
-    chunkc::cp_async_commit();
   };
   // per-token decay and beta of job J into warp 0's registers
   auto scalars_in = [&](const Job& J, float (&x)[4]) {
@@ -214,11 +227,11 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
   Job cur = job_of(p, j < njobs ? j : 0);
   if (j >= njobs) cur.clen = 0;
   float sc_cur[4], sc_next[4];
+  tc::fence_before_sync();
+  __syncthreads();  // barriers initialised before the first load
+  tc::fence_after_sync();
   stage_in(cur, 0);
   scalars_in(cur, sc_cur);
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
   const uint32_t tm = tmem_slot;
   const uint32_t tq = tc::tmem_addr(tm, quarter * 32, 0);
   const uint32_t id_gram = tc::idesc_f16(128, 64, kBf16);
@@ -237,7 +250,26 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
     const Job J = cur;
     if (J.clen > 0) {
       uint8_t* rec = p.ws + (((int64_t)J.n * p.W + J.cw) * HV + J.hv) * (int64_t)REC_BYTES;
-      asm volatile("cp.async.wait_group 1;" ::: "memory");  // this job's stage landed
+      {  // this job's stage landed (warp 0 polls); rows past clen -> zero
+        const bool ok = warp != 0 || tc::mbar_wait(&in_bar[st], (in_phase >> st) & 1u);
+        if (__syncthreads_or(!ok)) {  // still pending: waited for once more below
+          if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+          break;
+        }
+        in_phase ^= 1u << st;
+        in_pending &= ~(1u << st);
+        if (J.clen < CH) {
+          const int nz = CH - J.clen;  // rows per box to clear, 8 x 16 bytes each
+          for (int e = tid; e < 6 * nz * 8; e += WY_THREADS) {
+            const int box = e / (nz * 8), rest = e - box * nz * 8;
+            const int row = J.clen + (rest >> 3);
+            const uint32_t off = box < 4 ? ST_QK + (box >> 1) * 2 * BOX + (box & 1) * BOX
+                                         : ST_V + (box - 4) * BOX;
+            *reinterpret_cast<uint4*>(sg + off + row * 128 + (rest & 7) * 16) =
+                make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
       if (warp == 0) {  // inclusive decay scan
         float a = sc_cur[0], b = sc_cur[1];
         s_beta[lane] = sc_cur[2];
@@ -265,11 +297,12 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
       // ---- MMA 1: [k; q] x k^T -> D1 (16-bit operands: the products of
       //      16-bit inputs are exact in the fp32 accumulator)
       if (tid == 0) {
-        const uint64_t x0 = tc::smem_desc(tc::smem_u32(sg + ST_QK), LBO, SBO_H);
+        const uint64_t x0 = tc::smem_desc_sw128(tc::smem_u32(sg + ST_QK));
 #pragma unroll
-        for (int kk = 0; kk < KD / 16; ++kk)
-          tc::mma_f16(tm + T_D1, tc::desc_add(x0, kk * KSTEP), tc::desc_add(x0, kk * KSTEP),
-                      id_gram, kk > 0);
+        for (int kk = 0; kk < KD / 16; ++kk) {  // 16 elements (32 bytes) of K per MMA
+          const uint64_t x = tc::desc_add(x0, (kk >> 2) * 2 * BOX + (kk & 3) * 32);
+          tc::mma_f16(tm + T_D1, x, x, id_gram, kk > 0);
+        }
         tc::mma_commit(&mbar);
       }
       {  // squared norms per row (thread: half a row)
@@ -277,7 +310,7 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
         float ss = 0.f;
 #pragma unroll
         for (int pc = 0; pc < 8; ++pc) {
-          const uint4 u = *reinterpret_cast<const uint4*>(sg + ST_QK + hoff(r, half * 64 + pc * 8));
+          const uint4 u = *reinterpret_cast<const uint4*>(sg + qk_off(r, half * 64 + pc * 8));
           const Tin* e = reinterpret_cast<const Tin*>(&u);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -300,7 +333,7 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int s = s0 + i;
-          x[i] = s_beta[s] * to_f32(reinterpret_cast<const Tin*>(sg + ST_V + s * V_ROW)[l]);
+          x[i] = s_beta[s] * to_f32(*reinterpret_cast<const Tin*>(sg + v_off(s, l)));
         }
         tc::tmem_st32(tq + T_AV + s0, x);
         float y[32];
@@ -308,7 +341,7 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
         for (int i = 0; i < 32; ++i) {
           const int s = s0 + i;
           const float kv =
-              to_f32(*reinterpret_cast<const Tin*>(sg + ST_QK + hoff(s, l))) * s_rk[s];
+              to_f32(*reinterpret_cast<const Tin*>(sg + qk_off(s, l))) * s_rk[s];
           x[i] = s_beta[s] * s_eG[s] * kv;
           y[i] = s_eGC[s] * kv;
         }
@@ -323,7 +356,7 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
         for (int jj = 0; jj < 4; ++jj) {
           const int e = tid + WY_THREADS * jj;
           const int t = (e >> 7) * 8 + (e & 7), k8 = ((e >> 3) & 15) * 8;
-          const uint4 u = *reinterpret_cast<const uint4*>(sg + ST_QK + hoff(64 + t, k8));
+          const uint4 u = *reinterpret_cast<const uint4*>(sg + qk_off(64 + t, k8));
           const Tin* h = reinterpret_cast<const Tin*>(&u);
           const float f = s_rq[t] * s_eG[t];
           uint8_t* dst = rec + R_WQ + 32768;
@@ -435,7 +468,11 @@ __global__ void __launch_bounds__(WY_THREADS, 2) gdn_wy_kernel(WyArgs p, int njo
     for (int i = 0; i < 4; ++i) sc_cur[i] = sc_next[i];
   }
 
-  chunkc::cp_async_wait_all();
+  // no TMA load may still target this CTA's shared memory
+  for (int st = 0; st < 2; ++st)
+    if (((in_pending >> st) & 1u) && warp == 0 &&
+        !tc::mbar_wait(&in_bar[st], (in_phase >> st) & 1u) && lane == 0)
+      report(p.status, WKVM_ERR_TIMEOUT);
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tm, WY_TMEM_COLS);
@@ -696,6 +733,14 @@ template <typename Tin>
 int run_windows(const WyArgs& wa0, const int32_t* ids, int64_t num_slots, const float* h_in, float* h_out, bool slots, float* carry,
                 void* o, int nseq, int64_t max_chunks, int64_t W, cudaStream_t stream) {
   auto k1 = gdn_wy_kernel<Tin>;
+  WyMaps maps;
+  const int64_t tokens = wa0.cu ? (int64_t)wa0.T : (int64_t)nseq * wa0.T;
+  if (tokens > 0) {
+    int rc = tma::encode_rows(&maps.q, wa0.q, tokens, wa0.H, KD, CH);
+    if (rc == WKVM_OK) rc = tma::encode_rows(&maps.k, wa0.k, tokens, wa0.H, KD, CH);
+    if (rc == WKVM_OK) rc = tma::encode_rows(&maps.v, wa0.v, tokens, wa0.HV, VD, CH);
+    if (rc != WKVM_OK) return rc;
+  }
   auto k2 = gdn_state_kernel<Tin>;
   int dev = 0, num_sms = 148;
   WKVM_CUDA_TRY(cudaGetDevice(&dev));
@@ -714,7 +759,7 @@ int run_windows(const WyArgs& wa0, const int32_t* ids, int64_t num_slots, const 
     if (wn > 0) {
       const int njobs = (int)(wn * nseq * a.HV);
       const int grid = njobs < 2 * num_sms ? njobs : 2 * num_sms;
-      k1<<<grid, WY_THREADS, WY_SMEM, stream>>>(a, njobs);
+      k1<<<grid, WY_THREADS, WY_SMEM, stream>>>(a, njobs, maps);
     }
     k2<<<dim3(nseq, a.HV), ST_THREADS, ST_SMEM, stream>>>(sa);
     WKVM_CUDA_TRY(cudaGetLastError());

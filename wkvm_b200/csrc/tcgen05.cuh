@@ -32,6 +32,20 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 
+// Shared-memory matrix descriptor of a K-major operand in the 128-byte
+// swizzled layout that TMA writes (rows of 128 bytes, 8-row atoms of 1024
+// bytes, 1024-byte aligned): SBO = 1024 between 8-row groups; the K offset
+// within the 128-byte row is added to the start address (desc_add).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
+  d |= (uint64_t)1 << 16;                   // LBO: unused for swizzled K-major
+  d |= (uint64_t)(1024 >> 4) << 32;         // SBO
+  d |= (uint64_t)1 << 46;                   // descriptor version
+  d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
+  return d;
+}
+
 // The descriptor of an operand `bytes` further on in shared memory (the start
 // address field counts 16-byte units; `bytes` keeps it inside the 256 KiB
 // window). MMA issue loops step a base descriptor with this instead of

@@ -34,13 +34,13 @@ EncodeFn encode_fn() {
 int encode_rows(CUtensorMap* map, const void* base, int64_t tokens, int heads, int D, int rows) {
   EncodeFn fn = encode_fn();
   if (!fn) return WKVM_ERR_CUDA;
-  if (D * 2 != 128 || rows <= 0 || rows > 256 || tokens <= 0 || heads <= 0)
+  if (D <= 0 || D % 64 || rows <= 0 || rows > 256 || tokens <= 0 || heads <= 0)
     return WKVM_ERR_INVALID_ARG;
   if (reinterpret_cast<uintptr_t>(base) & 15u) return WKVM_ERR_ALIGN;
   const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)tokens};
   // byte strides of dims 1 and 2 (multiples of 16)
   const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2};
-  const cuuint32_t box[3] = {(cuuint32_t)D, 1u, (cuuint32_t)rows};
+  const cuuint32_t box[3] = {64u, 1u, (cuuint32_t)rows};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,

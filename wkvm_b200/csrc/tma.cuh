@@ -29,15 +29,16 @@ __device__ __forceinline__ uint32_t sw128_off(int t, uint32_t b) {
   return (uint32_t)t * 128u + ((((b >> 4) ^ (uint32_t)t) & 7u) << 4) + (b & 15u);
 }
 
-// 3-D tiled load (no multicast) of box {D, 1, rows} at (0, head, token0)
-// into `dst` (1024-byte aligned), counted on `mbar`.
+// 3-D tiled load (no multicast) of box {64, 1, rows} at (col0, head,
+// token0) into `dst` (1024-byte aligned), counted on `mbar`. col0 is a
+// multiple of 64 elements (128 bytes), so the box starts 16-byte aligned.
 __device__ __forceinline__ void load_rows(void* dst, const CUtensorMap* map, int head, int token0,
-                                          uint64_t* mbar) {
+                                          uint64_t* mbar, int col0 = 0) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4}], [%5];"
       :: "r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(reinterpret_cast<uint64_t>(map)),
-         "r"(0), "r"(head), "r"(token0), "r"((uint32_t)__cvta_generic_to_shared(mbar))
+         "r"(col0), "r"(head), "r"(token0), "r"((uint32_t)__cvta_generic_to_shared(mbar))
       : "memory");
 }
 
@@ -45,8 +46,9 @@ __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// Host: describes a [tokens, heads, D] tensor of 16-bit elements (D * 2 ==
-// 128 bytes) for boxes of `rows` tokens of one head. Returns 0 on success.
+// Host: describes a [tokens, heads, D] tensor of 16-bit elements (D a
+// multiple of 64) for boxes of `rows` tokens x 64 elements of one head.
+// Returns 0 on success.
 int encode_rows(CUtensorMap* map, const void* base, int64_t tokens, int heads, int D, int rows);
 
 }  // namespace tma
