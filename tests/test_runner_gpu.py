@@ -149,3 +149,53 @@ def test_runner_matches_wkvm_flow(cuda, fuse):
         assert ours.wkv[:, s].abs().sum().item() == 0.0
     for s in (0, 1, 3, 4, 5):
         assert ours.shift[:, :, s].abs().sum().item() == 0.0
+
+
+@pytest.mark.parametrize("fuse", [True, False])
+def test_graphed_decode_matches_wkvm_flow(cuda, fuse):
+    """The whole decode step captured once (wkvm_b200.graph.GraphedDecode)
+    and replayed for changing batches -- full, and smaller than the graph
+    (padded with slot 0) -- against wkvm's gather -> fla Triton -> scatter
+    flow on the same states."""
+    from wkvm_b200 import fla_compat
+    from wkvm_b200.graph import GraphedDecode
+    from wkvm_b200.runner import RWKV7Runner
+
+    torch.manual_seed(1)
+    L, D, N, vocab = 2, 256, 64, 512
+    cfg = fla_models.RWKV7Config(hidden_size=D, num_hidden_layers=L, head_dim=N,
+                                 vocab_size=vocab)
+    with torch.device(cuda):
+        model = fla_models.RWKV7ForCausalLM(cfg)
+    model = model.to(torch.bfloat16).eval()
+    ours = _bank(cuda, n_layer=L, D=D, N=N, slots=8)
+    g = torch.Generator(device=cuda).manual_seed(2)
+    ours.wkv.normal_(0.0, 0.1, generator=g)
+    ours.shift.copy_(torch.randn(ours.shift.shape, generator=g, device=cuda) * 0.5)
+    stock = StockBank(ours)
+    stock.wkv.copy_(ours.wkv)
+    stock.shift.copy_(ours.shift)
+    batches = [[{"wkv": 3, "shift": 3}, {"wkv": 7, "shift": 5}, {"wkv": 1, "shift": 8}],
+               [{"wkv": 7, "shift": 5}, {"wkv": 2, "shift": 2}],
+               [{"wkv": 1, "shift": 8}, {"wkv": 3, "shift": 3}, {"wkv": 8, "shift": 1}]]
+    gen = torch.Generator().manual_seed(5)
+    toks = [torch.randint(0, vocab, (len(b),), generator=gen).tolist() for b in batches]
+    fla_compat.uninstall()
+    ref_runner = RWKV7Runner(model, stock)
+    ref = [ref_runner.decode_step(b, t) for b, t in zip(batches, toks)]
+    try:
+        gd = GraphedDecode(RWKV7Runner(model, ours), batch_size=3, fuse_time_mix=fuse)
+        got = [gd.decode_step(b, t) for b, t in zip(batches, toks)]
+        torch.cuda.synchronize()
+    finally:
+        fla_compat.uninstall()
+    for i, (o, r) in enumerate(zip(got, ref)):
+        assert o.shape == r.shape, i
+        assert rel_err(o, r) < 2e-2, i
+        assert (o.argmax(-1) == r.argmax(-1)).all(), i
+    used_wkv = [1, 2, 3, 7, 8]
+    used_shift = [1, 2, 3, 5, 8]
+    assert rel_err(ours.wkv[:, used_wkv], stock.wkv[:, used_wkv]) < 2e-2
+    assert rel_err(ours.shift[:, :, used_shift].float(), stock.shift[:, :, used_shift].float()) < 2e-2
+    for s in (4, 5, 6):  # never in a batch: untouched
+        assert torch.equal(ours.wkv[:, s], stock.wkv[:, s])
