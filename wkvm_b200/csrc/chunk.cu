@@ -229,13 +229,13 @@ dplr_chunk_kernel(ChunkArgs p, const __grid_constant__ InMaps maps) {
   const uint32_t idesc64 = tc::idesc_tf32(128, 64);
   const uint32_t idesc128 = tc::idesc_tf32(128, 128);
 
-  // Thread 0 issues the TMA loads of chunk c's six 64 x 64 input tiles (one
+  // Lane 0 of the last warp issues the TMA loads of chunk c's six 64 x 64 input tiles (one
   // box per stream, no multicast), counted on tma_bar. Rows past the end of
   // the sequence are zeroed after they land (see the loop head).
   uint32_t tphase = 0;
   bool tma_pending = false;
   auto stage = [&](int c) {
-    if (tid == 0) {
+    if (tid == NTHREADS - 32) {  // off warp 0, which issues the MMAs and polls their barrier
       tc::mbar_expect_tx(&tma_bar, NIN * STG_TILE);
       const int tok = (int)(bos + (int64_t)c * CH);
 #pragma unroll

@@ -10,8 +10,9 @@
 //      U = T (beta v),  W = T (beta e^G k^)                     (u = U - W S)
 //      Q~ = scale e^G q^,  K~ = e^(G_C-G) k^,
 //      A_qk[t][s] = scale e^(G_t-G_s) q^_t.k^_s (s <= t)
-//  phase 2, gdn_state_kernel: one CTA per (sequence, value head) walks the
-//    chunks in order with the state S^T (rows v, columns k) resident in TMEM:
+//  phase 2, gdn_state_kernel: two CTAs per (sequence, value head), one per
+//    half of the value columns, walk the chunks in order with their half of
+//    the state S^T (64 rows v, columns k) resident in TMEM (M = 64 tiles):
 //      [(W S)^T | (Q~ S)^T] = S^T [W; Q~]^T                    (MMA A)
 //      u^T = U^T - (W S)^T,  S^T <- e^(G_C) S^T
 //      S^T += u^T K~,  (Q~ S)^T += u^T A_qk^T = O^T            (MMA B)
@@ -42,12 +43,14 @@ constexpr uint32_t KSTEP = 2 * LBO;              // 8 tf32 of K per MMA
 constexpr uint32_t R_WQ = 0;                 // [W; Q~]: 128 rows x K = 128 (k), SBO 4096
 constexpr uint32_t R_KT = R_WQ + 65536;      // K~^T: 128 rows (k) x K = 64 (t), SBO 2048
 constexpr uint32_t R_AQK = R_KT + 32768;     // A_qk: 64 rows (t) x K = 64 (s), SBO 2048
-constexpr uint32_t R_U = R_AQK + 16384;      // U: 64 rows (t) x 128 v, row-major
+constexpr uint32_t R_U = R_AQK + 16384;      // U: two v-halves, each 64 rows (t) x 64 v
 constexpr uint32_t R_META = R_U + 32768;     // e^(G_C)
 constexpr uint32_t REC_BYTES = R_META + 128;
-constexpr uint32_t PART_A = R_KT - R_WQ;             // loaded first (MMA A)
-constexpr uint32_t PART_B = R_META + 16 - R_KT;      // the rest
-static_assert(REC_BYTES % 128 == 0 && PART_B % 16 == 0, "record alignment");
+constexpr uint32_t PART_A = R_KT - R_WQ;             // [W; Q~]: MMA A
+constexpr uint32_t PART_B = R_U - R_KT;              // K~^T and A_qk: MMA B
+constexpr uint32_t PART_U = 64 * 64 * 4;            // one v-half of U: the u pass
+static_assert(REC_BYTES % 128 == 0 && PART_B % 16 == 0 && PART_U % 16 == 0,
+              "record alignment");
 
 }  // namespace gdnwy
 
@@ -190,13 +193,14 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
     tma::prefetch_map(&maps.v);
   }
 
-  // TMA loads of job J's k, q, v rows into stage st (thread 0; nothing for a
+  // TMA loads of job J's k, q, v rows into stage st (one thread of the last
+  // warp, off warp 0's barrier polls; nothing for a
   // job past its sequence's end). Rows past clen are zeroed once they land.
   uint32_t in_phase = 0u, in_pending = 0u;  // bit st: stage st's parity / a load in flight
   auto stage_in = [&](const Job& J, int st) {
     if (J.clen <= 0) return;
     in_pending |= 1u << st;
-    if (tid != 0) return;
+    if (tid != WY_THREADS - 32) return;  // lane 0 of the last warp: warp 0 polls barriers
     uint8_t* base = sm + st * STAGE;
     const int hq = J.hv / (HV / H);
     const int tok = (int)J.tok0;
@@ -435,9 +439,9 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
         const int t0 = gh * 32;
         float x[32];
         tc::tmem_ld32(tq + T_D1 + t0, x);  // U^T[v = l][t0 + i] -> U[t][v], 128 B per warp and t
-        float* ucol = reinterpret_cast<float*>(rec + R_U) + l;
+        float* ucol = reinterpret_cast<float*>(rec + R_U) + (l >> 6) * 64 * 64 + (l & 63);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) ucol[(t0 + i) * VD] = x[i];
+        for (int i = 0; i < 32; ++i) ucol[(t0 + i) * 64] = x[i];
         // W^T[k = l][t0 + i] -> row-major W[t][k] in the spent stage (row
         // stride W_ROW: lanes hit distinct banks), copied out below
         tc::tmem_ld32(tq + T_DW + t0, x);
@@ -480,11 +484,17 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
 
 // ---------------------------------------------------------------- phase 2
 
+// Two CTAs per (sequence, value head): CTA vh owns value columns
+// [64 vh, 64 vh + 64), so a sequence-head's chain runs on two SMs and each
+// CTA issues M = 64 MMAs. An M = 64 tile occupies TMEM lanes 0..15 of each
+// 32-lane quarter (row r at lane 32 (r / 16) + r % 16), for accumulators and
+// for A operands alike, so lanes 16..31 of every warp carry no data.
 constexpr int ST_THREADS = 256;  // two warps per TMEM lane quarter
-constexpr uint32_t SS_A0 = 0, SS_A1 = PART_A, SS_B = 2 * PART_A;
-constexpr uint32_t ST_SMEM = SS_B + PART_B + 1024;
+constexpr uint32_t SS_A0 = 0, SS_A1 = PART_A, SS_B = 2 * PART_A, SS_U = SS_B + PART_B;
+constexpr uint32_t SS_M = SS_U + PART_U;  // e^(G_C)
+constexpr uint32_t ST_SMEM = SS_M + 128 + 1024;
 static_assert(ST_SMEM <= 227 * 1024, "shared memory budget");
-// TMEM: S^T (128 columns), two MMA A accumulators, u^T (A operand of MMA B)
+// TMEM: S^T half (128 columns), two MMA A accumulators, u^T (A operand of MMA B)
 constexpr uint32_t ST_TMEM_COLS = 512;
 constexpr uint32_t T_S = 0, T_DA0 = 128, T_DA1 = 256, T_U = 384;
 
@@ -492,19 +502,21 @@ template <typename Tin>
 __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  __shared__ uint64_t mb_a[2], mb_b, mb_m;
+  __shared__ uint64_t mb_a[2], mb_b, mb_u, mb_m;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int v = (warp & 3) * 32 + lane;  // TMEM lane = value column
-  const int gq = warp >> 2;              // which half of t / k this thread takes
-  const int n = blockIdx.x, hv = blockIdx.y;
+  const bool live = lane < 16;                // a lane of the M = 64 tile
+  const int vl = (warp & 3) * 16 + (lane & 15);  // value column within the half
+  const int gq = warp >> 2;                   // which half of t / k this thread takes
+  const int n = blockIdx.x, hv = blockIdx.y, vh = blockIdx.z;
+  const int v = vh * 64 + vl;
   const int HV = p.HV;
   int64_t row = n;
   if (p.ids) {
     const int32_t id = p.ids[n];
     if (id < 0 || (int64_t)id >= p.num_slots) {
-      if (tid == 0) report(p.status, WKVM_ERR_SLOT_RANGE);
+      if (tid == 0 && vh == 0) report(p.status, WKVM_ERR_SLOT_RANGE);
       return;
     }
     row = id;
@@ -523,10 +535,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
   const int cend = nch < p.w0 + p.W ? nch : p.w0 + p.W;
   const int cnt = cend - p.w0;
   const bool same = p.h_src == p.h_dst && soff == doff;
-  if (cnt <= 0) {  // nothing in this window: carry the state over
+  if (cnt <= 0) {  // nothing in this window: carry this half of the state over
     if (p.h_dst && !same)
-      for (int e = tid; e < KD * VD; e += ST_THREADS)
-        p.h_dst[doff + e] = p.h_src ? p.h_src[soff + e] : 0.f;
+      for (int e = tid; e < KD * 64; e += ST_THREADS) {
+        const int64_t o = (e >> 6) * VD + vh * 64 + (e & 63);
+        p.h_dst[doff + o] = p.h_src ? p.h_src[soff + o] : 0.f;
+      }
     return;
   }
   const uint8_t* recs = p.ws + ((int64_t)n * p.W * HV + hv) * (int64_t)REC_BYTES;
@@ -541,6 +555,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     tc::mbar_init(&mb_a[0], 1);
     tc::mbar_init(&mb_a[1], 1);
     tc::mbar_init(&mb_b, 1);
+    tc::mbar_init(&mb_u, 1);
     tc::mbar_init(&mb_m, 1);
     tc::fence_mbar_init();
   }
@@ -550,12 +565,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
   const uint32_t tm = tmem_slot;
   const uint32_t tq = tc::tmem_addr(tm, (warp & 3) * 32, 0);
 
-  // S^T[v][k] = h[k][v]
+  // S^T[v][k] = h[k][v] for this half's v
 #pragma unroll 1
   for (int kb = gq * 64; kb < gq * 64 + 64; kb += 32) {
     float x[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) x[i] = p.h_src ? p.h_src[soff + (kb + i) * VD + v] : 0.f;
+    for (int i = 0; i < 32; ++i)
+      x[i] = (live && p.h_src) ? p.h_src[soff + (kb + i) * VD + v] : 0.f;
     tc::tmem_st32(tq + T_S + kb, x);
   }
   tc::tmem_st_wait();
@@ -564,8 +580,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
   __syncthreads();
   tc::fence_after_sync();
 
-  uint32_t ph_a[2] = {0, 0}, ph_b = 0, ph_m = 0;
-  int pend_a[2] = {0, 0}, pend_b = 0;  // copies issued and not yet waited for
+  uint32_t ph_a[2] = {0, 0}, ph_b = 0, ph_u = 0, ph_m = 0;
+  int pend_a[2] = {0, 0}, pend_b = 0, pend_u = 0;  // copies issued and not yet waited for
   auto issue_a = [&](int i) {
     const int b = i & 1;
     tc::mbar_expect_tx(&mb_a[b], PART_A);
@@ -575,14 +591,21 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     tc::mbar_expect_tx(&mb_b, PART_B);
     tc::bulk_g2s(sm + SS_B, recs + i * rstride + R_KT, PART_B, &mb_b);
   };
+  auto issue_u = [&](int i) {  // this half of U, and e^(G_C)
+    tc::mbar_expect_tx(&mb_u, PART_U + 16);
+    tc::bulk_g2s(sm + SS_U, recs + i * rstride + R_U + vh * PART_U, PART_U, &mb_u);
+    tc::bulk_g2s(sm + SS_M, recs + i * rstride + R_META, 16, &mb_u);
+  };
   if (tid == 0) {
     issue_a(0);
-    if (cnt > 1) issue_a(1);
+    issue_u(0);
     issue_b(0);
+    if (cnt > 1) issue_a(1);
   }
   pend_a[0] = 1;
   pend_a[1] = cnt > 1;
   pend_b = 1;
+  pend_u = 1;
 
   // O^T of chunk i (accumulator da) -> o rows t in this thread's half. Lane
   // pairs swap values so that each store writes two adjacent columns: the
@@ -605,7 +628,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
       union { uint32_t u; Tin e[2]; } pk;
       pk.e[0] = from_f32<Tin>(odd ? other : mine);
       pk.e[1] = from_f32<Tin>(odd ? mine : other);
-      if (t < clen) *reinterpret_cast<uint32_t*>(col + (int64_t)t * HV * VD) = pk.u;
+      if (live && t < clen) *reinterpret_cast<uint32_t*>(col + (int64_t)t * HV * VD) = pk.u;
     }
   };
 
@@ -621,6 +644,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     if (!bad) ph ^= 1u;
     return !bad;
   };
+  const uint32_t id_a = tc::idesc_tf32(64, 128), id_s = tc::idesc_tf32(64, 128),
+                 id_o = tc::idesc_tf32(64, 64);
 
 #pragma unroll 1
   for (int i = 0; i < cnt; ++i) {
@@ -633,19 +658,18 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
       ok = tc::mbar_wait(&mb_a[b], ph_a[b]);
       if (ok) {  // MMA A: S^T x [W; Q~]^T
         const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + (b ? SS_A1 : SS_A0)), LBO, SBO128);
-        const uint32_t id = tc::idesc_tf32(128, 128);
 #pragma unroll
         for (int kk = 0; kk < KD / 8; ++kk)
-          tc::mma_tf32_ta(tm + da, tm + T_S + kk * 8, tc::desc_add(a0, kk * KSTEP), id, kk > 0);
+          tc::mma_tf32_ta(tm + da, tm + T_S + kk * 8, tc::desc_add(a0, kk * KSTEP), id_a, kk > 0);
         tc::mma_commit(&mb_m);
       }
     }
     mma_inflight = true;
     if (i > 0) output(i - 1, b ? T_DA0 : T_DA1);  // overlaps MMA A
-    // warp 0 waits for MMA A and for the U / K~ / A_qk copy; one barrier
+    // warp 0 waits for MMA A and for the U copy; one barrier
     if (warp == 0) {
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      ok = ok && tc::mbar_wait(&mb_m, ph_m) && tc::mbar_wait(&mb_b, ph_b);
+      ok = ok && tc::mbar_wait(&mb_m, ph_m) && tc::mbar_wait(&mb_u, ph_u);
     }
     if (__syncthreads_or(!ok)) {
       if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
@@ -657,19 +681,22 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     pend_a[b] = 0;
     ph_m ^= 1u;
     mma_inflight = false;
-    ph_b ^= 1u;
-    pend_b = 0;
+    ph_u ^= 1u;
+    pend_u = 0;
+    // MMA A has read this buffer of [W; Q~]: chunk i+2's copy goes out now
+    if (tid == 0 && i + 2 < cnt) issue_a(i + 2);
+    if (i + 2 < cnt) pend_a[b] = 1;
     {  // u^T = U^T - (W S)^T ; S^T *= e^(G_C)
-      const float* ucol = reinterpret_cast<const float*>(sm + SS_B + (R_U - R_KT)) + v;
+      const float* ucol = reinterpret_cast<const float*>(sm + SS_U) + vl;
       {
         const int t0 = gq * 32;
         float x[32];
         tc::tmem_ld32(tq + da + t0, x);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) x[j] = ucol[(t0 + j) * VD] - x[j];
+        for (int j = 0; j < 32; ++j) x[j] = ucol[(t0 + j) * 64] - x[j];
         tc::tmem_st32(tq + T_U + t0, x);
       }
-      const float eg = *reinterpret_cast<const float*>(sm + SS_B + (R_META - R_KT));
+      const float eg = *reinterpret_cast<const float*>(sm + SS_M);
 #pragma unroll 1
       for (int kb = gq * 64; kb < gq * 64 + 64; kb += 32) {
         float x[32];
@@ -683,27 +710,35 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
+    // the u pass has read U: chunk i+1's U copy goes out; the issuer alone
+    // waits for this chunk's K~ / A_qk, which only the tensor core reads
+    if (tid == 0 && i + 1 < cnt) issue_u(i + 1);
+    if (i + 1 < cnt) pend_u = 1;
+    ok = tid != 0 || tc::mbar_wait(&mb_b, ph_b);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) report(p.status, WKVM_ERR_TIMEOUT);
+      failed = true;
+      break;
+    }
+    ph_b ^= 1u;
+    pend_b = 0;
     if (tid == 0) {  // MMA B: S^T += u^T K~ ; O^T += u^T A_qk^T
       const uint64_t k0 = tc::smem_desc(tc::smem_u32(sm + SS_B), LBO, SBO64);
       const uint64_t q0 = tc::desc_add(k0, R_AQK - R_KT);
-      const uint32_t id128 = tc::idesc_tf32(128, 128), id64 = tc::idesc_tf32(128, 64);
 #pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + T_S, tm + T_U + kk * 8, tc::desc_add(k0, kk * KSTEP), id128, true);
+        tc::mma_tf32_ta(tm + T_S, tm + T_U + kk * 8, tc::desc_add(k0, kk * KSTEP), id_s, true);
 #pragma unroll
       for (int kk = 0; kk < CH / 8; ++kk)
-        tc::mma_tf32_ta(tm + da + 64, tm + T_U + kk * 8, tc::desc_add(q0, kk * KSTEP), id64, true);
+        tc::mma_tf32_ta(tm + da + 64, tm + T_U + kk * 8, tc::desc_add(q0, kk * KSTEP), id_o, true);
       tc::mma_commit(&mb_m);
     }
     mma_inflight = true;
     if (!wait_all(&mb_m, ph_m)) { failed = true; break; }
     mma_inflight = false;
-    // the copy needed next goes out first: U / K~ / A_qk of chunk i+1, then
-    // [W; Q~] of chunk i+2 (MMA A and MMA B have read both buffers)
+    // MMA B has read K~ / A_qk: chunk i+1's copy goes out
     if (tid == 0 && i + 1 < cnt) issue_b(i + 1);
     if (i + 1 < cnt) pend_b = 1;
-    if (tid == 0 && i + 2 < cnt) issue_a(i + 2);
-    if (i + 2 < cnt) pend_a[b] = 1;
   }
 
   if (!failed) {
@@ -713,8 +748,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
       for (int kb = gq * 64; kb < gq * 64 + 64; kb += 32) {
         float x[32];
         tc::tmem_ld32(tq + T_S + kb, x);
+        if (live) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) p.h_dst[doff + (kb + i) * VD + v] = x[i];
+          for (int i = 0; i < 32; ++i) p.h_dst[doff + (kb + i) * VD + v] = x[i];
+        }
       }
     }
   } else {
@@ -722,6 +759,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     if (pend_a[0]) tc::mbar_wait(&mb_a[0], ph_a[0]);
     if (pend_a[1]) tc::mbar_wait(&mb_a[1], ph_a[1]);
     if (pend_b) tc::mbar_wait(&mb_b, ph_b);
+    if (pend_u) tc::mbar_wait(&mb_u, ph_u);
     if (mma_inflight) tc::mbar_wait(&mb_m, ph_m);
   }
   tc::fence_before_sync();
@@ -761,7 +799,7 @@ int run_windows(const WyArgs& wa0, const int32_t* ids, int64_t num_slots, const 
       const int grid = njobs < 2 * num_sms ? njobs : 2 * num_sms;
       k1<<<grid, WY_THREADS, WY_SMEM, stream>>>(a, njobs, maps);
     }
-    k2<<<dim3(nseq, a.HV), ST_THREADS, ST_SMEM, stream>>>(sa);
+    k2<<<dim3(nseq, a.HV, 2), ST_THREADS, ST_SMEM, stream>>>(sa);
     WKVM_CUDA_TRY(cudaGetLastError());
   }
   return WKVM_OK;
