@@ -149,6 +149,11 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
                :: "r"(smem_u32(mbar)), "r"(bytes) : "memory");
 }
 
+// Plain arrival on `mbar` (no transaction bytes).
+__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(mbar)) : "memory");
+}
+
 // Untiled bulk copy global -> this CTA's shared memory (no multicast); both
 // addresses 16-byte aligned, `bytes` a multiple of 16. Completion is counted
 // on `mbar` as transaction bytes.
