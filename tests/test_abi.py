@@ -86,9 +86,9 @@ def test_host_argument_checks(lib):
 
 
 def test_gdn_workspace_size(lib):
-    # one 147,584-byte chunk record per (sequence, value head, 64-token chunk)
-    assert lib.wkvm_gdn_chunk_workspace_bytes(4, 8192, 16, 128, 128) == 4 * 16 * 128 * 147584
-    assert lib.wkvm_gdn_chunk_workspace_bytes(1, 65, 2, 128, 128) == 2 * 2 * 147584
+    # one 73,856-byte chunk record per (sequence, value head, 64-token chunk)
+    assert lib.wkvm_gdn_chunk_workspace_bytes(4, 8192, 16, 128, 128) == 4 * 16 * 128 * 73856
+    assert lib.wkvm_gdn_chunk_workspace_bytes(1, 65, 2, 128, 128) == 2 * 2 * 73856
     assert lib.wkvm_gdn_chunk_workspace_bytes(2, 0, 2, 128, 128) == 0
     # shapes without the two-launch path
     assert lib.wkvm_gdn_chunk_workspace_bytes(4, 64, 16, 64, 64) == 0

@@ -36,19 +36,39 @@ namespace gdnwy {
 
 constexpr int CH = 64, KD = 128, VD = 128;
 constexpr uint32_t LBO = 128;
-constexpr uint32_t SBO64 = 2048, SBO128 = 4096;  // K = 64 / K = 128 tiles
+constexpr uint32_t SBO64 = 2048;                 // fp32 tile, K = 64
 constexpr uint32_t KSTEP = 2 * LBO;              // 8 tf32 of K per MMA
 
-// record layout (bytes)
-constexpr uint32_t R_WQ = 0;                 // [W; Q~]: 128 rows x K = 128 (k), SBO 4096
-constexpr uint32_t R_KT = R_WQ + 65536;      // K~^T: 128 rows (k) x K = 64 (t), SBO 2048
-constexpr uint32_t R_AQK = R_KT + 32768;     // A_qk: 64 rows (t) x K = 64 (s), SBO 2048
-constexpr uint32_t R_U = R_AQK + 16384;      // U: two v-halves, each 64 rows (t) x 64 v
-constexpr uint32_t R_META = R_U + 32768;     // e^(G_C)
+// record layout (bytes). Every matrix is fp16: the state pass multiplies
+// with kind::f16, whose 10-bit significand is the tf32 one; the values are
+// unit-scale (normalised q, k; decays <= 1; U = T (beta v)). The operand
+// tiles are K-major, no swizzle, 8-row x 16-byte core matrices, LBO 128.
+constexpr uint32_t SBOH64 = 1024, SBOH128 = 2048;  // fp16 tiles, K = 64 / K = 128
+constexpr uint32_t KSTEP16 = 2 * LBO;              // 16 fp16 of K per MMA
+constexpr uint32_t R_WQ = 0;                 // [W; Q~]: 128 rows x K = 128 (k)
+constexpr uint32_t R_KT = R_WQ + 32768;      // K~^T: 128 rows (k) x K = 64 (t)
+constexpr uint32_t R_AQK = R_KT + 16384;     // A_qk: 64 rows (t) x K = 64 (s)
+constexpr uint32_t R_U = R_AQK + 8192;       // U: two v-halves, each 64 rows (t) x 64 v
+constexpr uint32_t R_META = R_U + 16384;     // e^(G_C), fp32
 constexpr uint32_t REC_BYTES = R_META + 128;
 constexpr uint32_t PART_A = R_KT - R_WQ;             // [W; Q~]: MMA A
 constexpr uint32_t PART_B = R_U - R_KT;              // K~^T and A_qk: MMA B
-constexpr uint32_t PART_U = 64 * 64 * 4;            // one v-half of U: the u pass
+constexpr uint32_t PART_U = 64 * 64 * 2;            // one v-half of U: the u pass
+
+// Byte offset of element (row, k) in an fp16 K-major tile.
+__host__ __device__ constexpr uint32_t hoff16(int row, int k, uint32_t sbo) {
+  return (uint32_t)(row >> 3) * sbo + (uint32_t)(k >> 3) * LBO + (uint32_t)(row & 7) * 16 +
+         (uint32_t)(k & 7) * 2;
+}
+
+// Eight floats as fp16, one 16-byte store.
+__device__ __forceinline__ void st_h8(uint8_t* p, const float* x) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
 static_assert(REC_BYTES % 128 == 0 && PART_B % 16 == 0 && PART_U % 16 == 0,
               "record alignment");
 
@@ -351,11 +371,9 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
         }
         tc::tmem_st32(tq + T_AK + s0, x);
 #pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          chunkc::kst4(rec + R_KT, l, s0 + i, LBO, SBO64,
-                       make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]));
-        // Q~ (fp32 K-major, rows 64..127 of [W; Q~]): piece e -> row t = 8 g + (e & 7),
-        // 8 columns from (e >> 3) & 15; eight lanes fill 128 contiguous bytes
+        for (int i = 0; i < 32; i += 8) st_h8(rec + R_KT + hoff16(l, s0 + i, SBOH64), y + i);
+        // Q~ (rows 64..127 of [W; Q~]): piece e -> row t = 8 g + (e & 7), 8
+        // columns from (e >> 3) & 15; eight lanes fill 128 contiguous bytes
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           const int e = tid + WY_THREADS * jj;
@@ -363,13 +381,10 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
           const uint4 u = *reinterpret_cast<const uint4*>(sg + qk_off(64 + t, k8));
           const Tin* h = reinterpret_cast<const Tin*>(&u);
           const float f = s_rq[t] * s_eG[t];
-          uint8_t* dst = rec + R_WQ + 32768;
-          chunkc::kst4(dst, t, k8, LBO, SBO128,
-                       make_float4(to_f32(h[0]) * f, to_f32(h[1]) * f, to_f32(h[2]) * f,
-                                   to_f32(h[3]) * f));
-          chunkc::kst4(dst, t, k8 + 4, LBO, SBO128,
-                       make_float4(to_f32(h[4]) * f, to_f32(h[5]) * f, to_f32(h[6]) * f,
-                                   to_f32(h[7]) * f));
+          float qv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) qv[i] = to_f32(h[i]) * f;
+          st_h8(rec + R_WQ + hoff16(64 + t, k8, SBOH128), qv);
         }
         tc::tmem_st_wait();
       }
@@ -407,9 +422,7 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
             x[i] = s <= t ? f * s_rk[s] * __expf(Gt - s_G[s]) * x[i] : 0.f;
           }
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            chunkc::kst4(rec + R_AQK, t, s0 + i, LBO, SBO64,
-                         make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]));
+          for (int i = 0; i < 32; i += 8) st_h8(rec + R_AQK + hoff16(t, s0 + i, SBOH64), x + i);
         }
       }
       __syncthreads();
@@ -439,9 +452,9 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
         const int t0 = gh * 32;
         float x[32];
         tc::tmem_ld32(tq + T_D1 + t0, x);  // U^T[v = l][t0 + i] -> U[t][v], 128 B per warp and t
-        float* ucol = reinterpret_cast<float*>(rec + R_U) + (l >> 6) * 64 * 64 + (l & 63);
+        __half* ucol = reinterpret_cast<__half*>(rec + R_U) + (l >> 6) * 64 * 64 + (l & 63);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) ucol[(t0 + i) * 64] = x[i];
+        for (int i = 0; i < 32; ++i) ucol[(t0 + i) * 64] = __float2half_rn(x[i]);
         // W^T[k = l][t0 + i] -> row-major W[t][k] in the spent stage (row
         // stride W_ROW: lanes hit distinct banks), copied out below
         tc::tmem_ld32(tq + T_DW + t0, x);
@@ -455,11 +468,14 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
          // matrix row group, a warp 512 contiguous bytes
         const float* wst = reinterpret_cast<const float*>(sg);
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
+        for (int jj = 0; jj < 4; ++jj) {
           const int e = tid + WY_THREADS * jj;
-          const int t = (e >> 8) * 8 + (e & 7), k4 = ((e >> 3) & 31) * 4;
-          *reinterpret_cast<float4*>(rec + R_WQ + tc::kmajor_off(t, k4, LBO, SBO128)) =
-              *reinterpret_cast<const float4*>(wst + t * W_ROW + k4);
+          const int t = (e >> 7) * 8 + (e & 7), k8 = ((e >> 3) & 15) * 8;
+          float wv[8];
+          *reinterpret_cast<float4*>(wv) = *reinterpret_cast<const float4*>(wst + t * W_ROW + k8);
+          *reinterpret_cast<float4*>(wv + 4) =
+              *reinterpret_cast<const float4*>(wst + t * W_ROW + k8 + 4);
+          st_h8(rec + R_WQ + hoff16(t, k8, SBOH128), wv);
         }
       }
       // the next job overwrites this stage only after every thread is past here
@@ -489,26 +505,39 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
 // CTA issues M = 64 MMAs. An M = 64 tile occupies TMEM lanes 0..15 of each
 // 32-lane quarter (row r at lane 32 (r / 16) + r % 16), for accumulators and
 // for A operands alike, so lanes 16..31 of every warp carry no data.
-// Warp roles: warps 0..7 (two per TMEM lane quarter) form u, rescale S and
-// write the outputs; warp 8 issues every copy and MMA and waits on the
-// mbarriers that gate them. The two sides meet only on mbarriers, so the
-// chain per chunk is MMA A -> u pass -> MMA B with no CTA-wide barrier.
+// Warp roles: warps 0..7 (two per TMEM lane quarter) form u, rescale S,
+// refresh the fp16 copy of S^T and write the outputs; warp 8 issues every
+// copy and MMA and waits on the mbarriers that gate them. The two sides meet
+// only on mbarriers, so the chain per chunk is MMA A -> u pass -> MMA B ->
+// fp16 copy of S^T, with no CTA-wide barrier. Both MMAs are kind::f16 (fp16
+// operands, the tf32 significand; fp32 accumulation): S^T itself stays fp32
+// in TMEM and the MMAs read its fp16 copy.
 constexpr int ST_WORKERS = 256;
 constexpr int ST_THREADS = ST_WORKERS + 32;
 constexpr uint32_t SS_A0 = 0, SS_A1 = PART_A, SS_B = 2 * PART_A, SS_U = SS_B + PART_B;
 constexpr uint32_t SS_M = SS_U + PART_U;  // e^(G_C)
 constexpr uint32_t ST_SMEM = SS_M + 128 + 1024;
 static_assert(ST_SMEM <= 227 * 1024, "shared memory budget");
-// TMEM: S^T half (128 columns), two MMA A accumulators, u^T (A operand of MMA B)
+// TMEM: S^T half (fp32, 128 columns), its fp16 copy (two k per column: A of
+// MMA A), u^T in fp16 (A of MMA B), two MMA A accumulators
 constexpr uint32_t ST_TMEM_COLS = 512;
-constexpr uint32_t T_S = 0, T_DA0 = 128, T_DA1 = 256, T_U = 384;
+constexpr uint32_t T_S = 0, T_S16 = 128, T_U16 = 192, T_DA0 = 256, T_DA1 = 384;
+
+// 32 floats as 16 columns of fp16 pairs (element 2c in the low half).
+__device__ __forceinline__ void pack_h16(const float (&x)[32], float (&y)[16]) {
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    __half2 h = __floats2half2_rn(x[2 * c], x[2 * c + 1]);
+    y[c] = *reinterpret_cast<float*>(&h);
+  }
+}
 
 template <typename Tin>
 __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   // copies: [W; Q~] x2, K~ / A_qk, U; MMA A done, MMA B done, u pass done
-  __shared__ uint64_t mb_a[2], mb_b, mb_u, mb_ma, mb_mb, mb_w;
+  __shared__ uint64_t mb_a[2], mb_b, mb_u, mb_ma, mb_mb, mb_w, mb_c;
   __shared__ uint32_t tmem_slot;
   __shared__ int s_fail;
 
@@ -567,6 +596,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     tc::mbar_init(&mb_ma, 1);
     tc::mbar_init(&mb_mb, 1);
     tc::mbar_init(&mb_w, ST_WORKERS / 32);
+    tc::mbar_init(&mb_c, ST_WORKERS / 32);
     tc::fence_mbar_init();
     s_fail = 0;
   }
@@ -576,15 +606,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
   const uint32_t tm = tmem_slot;
   const uint32_t tq = tc::tmem_addr(tm, (warp & 3) * 32, 0);
 
-  // S^T[v][k] = h[k][v] for this half's v
+  // S^T[v][k] = h[k][v] for this half's v, and its fp16 copy
   if (!issuer_warp) {
 #pragma unroll 1
     for (int kb = gq * 64; kb < gq * 64 + 64; kb += 32) {
-      float x[32];
+      float x[32], y[16];
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         x[i] = (live && p.h_src) ? p.h_src[soff + (kb + i) * VD + v] : 0.f;
       tc::tmem_st32(tq + T_S + kb, x);
+      pack_h16(x, y);
+      tc::tmem_st16(tq + T_S16 + kb / 2, y);
     }
     tc::tmem_st_wait();
   }
@@ -618,24 +650,24 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
       issue_u(0);
       issue_b(0);
       if (cnt > 1) issue_a(1);
-      const uint32_t id_a = tc::idesc_tf32(64, 128), id_o = tc::idesc_tf32(64, 64);
+      const uint32_t id_a = tc::idesc_f16(64, 128, false), id_o = tc::idesc_f16(64, 64, false);
       bool ok = true;
 #pragma unroll 1
       for (int i = 0; i < cnt && ok; ++i) {
         const int b = i & 1;
         const uint32_t da = b ? T_DA1 : T_DA0;
-        // MMA A: S^T x [W; Q~]^T, once this chunk's [W; Q~] landed (S^T is
-        // final: MMA B of the previous chunk completed below)
+        // MMA A: S^T x [W; Q~]^T, once this chunk's [W; Q~] landed (the fp16
+        // copy of S^T is current: the workers refreshed it after MMA B)
         if (!(ok = tc::mbar_wait(&mb_a[b], ph_a[b]))) break;
         ph_a[b] ^= 1u;
         pend_a[b] = 0;
         tc::fence_after_sync();
         {
-          const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + (b ? SS_A1 : SS_A0)), LBO, SBO128);
+          const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + (b ? SS_A1 : SS_A0)), LBO, SBOH128);
 #pragma unroll
-          for (int kk = 0; kk < KD / 8; ++kk)
-            tc::mma_tf32_ta(tm + da, tm + T_S + kk * 8, tc::desc_add(a0, kk * KSTEP), id_a,
-                            kk > 0);
+          for (int kk = 0; kk < KD / 16; ++kk)
+            tc::mma_f16_ta(tm + da, tm + T_S16 + kk * 8, tc::desc_add(a0, kk * KSTEP16), id_a,
+                           kk > 0);
           tc::mma_commit(&mb_ma);
           pend_m = 1;
         }
@@ -650,20 +682,21 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
         if (!(ok = tc::mbar_wait(&mb_b, ph))) break;
         pend_b = 0;
         {
-          const uint64_t k0 = tc::smem_desc(tc::smem_u32(sm + SS_B), LBO, SBO64);
+          const uint64_t k0 = tc::smem_desc(tc::smem_u32(sm + SS_B), LBO, SBOH64);
           const uint64_t q0 = tc::desc_add(k0, R_AQK - R_KT);
 #pragma unroll
-          for (int kk = 0; kk < CH / 8; ++kk)
-            tc::mma_tf32_ta(tm + T_S, tm + T_U + kk * 8, tc::desc_add(k0, kk * KSTEP), id_a,
-                            true);
+          for (int kk = 0; kk < CH / 16; ++kk)
+            tc::mma_f16_ta(tm + T_S, tm + T_U16 + kk * 8, tc::desc_add(k0, kk * KSTEP16), id_a,
+                           true);
 #pragma unroll
-          for (int kk = 0; kk < CH / 8; ++kk)
-            tc::mma_tf32_ta(tm + da + 64, tm + T_U + kk * 8, tc::desc_add(q0, kk * KSTEP), id_o,
-                            true);
+          for (int kk = 0; kk < CH / 16; ++kk)
+            tc::mma_f16_ta(tm + da + 64, tm + T_U16 + kk * 8, tc::desc_add(q0, kk * KSTEP16),
+                           id_o, true);
           tc::mma_commit(&mb_mb);
           pend_m = 1;
         }
-        if (!(ok = tc::mbar_wait(&mb_mb, ph))) break;
+        // the workers saw MMA B complete and refreshed the fp16 S^T
+        if (!(ok = tc::mbar_wait(&mb_c, ph))) break;
         pend_m = 0;
         tc::fence_after_sync();
         ph ^= 1u;
@@ -730,30 +763,43 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
     for (int i = 0; i < cnt; ++i) {
       const uint32_t da = (i & 1) ? T_DA1 : T_DA0;
       if (!wait_warp(&mb_ma, ph) || !wait_warp(&mb_u, ph)) break;
-      {  // u^T = U^T - (W S)^T ; S^T *= e^(G_C)
-        const float* ucol = reinterpret_cast<const float*>(sm + SS_U) + vl;
+      {  // u^T = U^T - (W S)^T in fp16 ; S^T *= e^(G_C)
+        const __half* ucol = reinterpret_cast<const __half*>(sm + SS_U) + vl;
         const int t0 = gq * 32;
-        float x[32];
+        float x[32], y[16];
         tc::tmem_ld32(tq + da + t0, x);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) x[j] = ucol[(t0 + j) * 64] - x[j];
-        tc::tmem_st32(tq + T_U + t0, x);
+        for (int j = 0; j < 32; ++j) x[j] = __half2float(ucol[(t0 + j) * 64]) - x[j];
+        pack_h16(x, y);
+        tc::tmem_st16(tq + T_U16 + t0 / 2, y);
         const float eg = *reinterpret_cast<const float*>(sm + SS_M);
 #pragma unroll 1
         for (int kb = gq * 64; kb < gq * 64 + 64; kb += 32) {
-          float y[32];
-          tc::tmem_ld32(tq + T_S + kb, y);
+          float z[32];
+          tc::tmem_ld32(tq + T_S + kb, z);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) y[j] *= eg;
-          tc::tmem_st32(tq + T_S + kb, y);
+          for (int j = 0; j < 32; ++j) z[j] *= eg;
+          tc::tmem_st32(tq + T_S + kb, z);
         }
         tc::tmem_st_wait();
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&mb_w);
-      // MMA B completes O^T of this chunk (and S^T for the next one)
+      // MMA B completes S^T for the next chunk (and O^T of this one): its
+      // fp16 copy first, then the outputs, which overlap the next MMA A
       if (!wait_warp(&mb_mb, ph)) break;
+#pragma unroll 1
+      for (int kb = gq * 64; kb < gq * 64 + 64; kb += 32) {
+        float z[32], y[16];
+        tc::tmem_ld32(tq + T_S + kb, z);
+        pack_h16(z, y);
+        tc::tmem_st16(tq + T_S16 + kb / 2, y);
+      }
+      tc::tmem_st_wait();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&mb_c);
       output(i, da);
       ph ^= 1u;
     }

@@ -125,6 +125,19 @@ __device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] x B[smem]^T with 16-bit operands (kind::f16): A read
+// from tensor memory with two consecutive K elements per 32-bit column (the
+// even one in the low half), issued by one thread.
+__device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                           uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      :: "r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+      : "memory");
+}
+
 // Arrives on `mbar` once every MMA issued so far by this thread completed.
 __device__ __forceinline__ void mma_commit(uint64_t* mbar) {
   asm volatile(
