@@ -393,6 +393,16 @@ def run_prefill(args, world, rank, local):
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(stop), world, dev)
     ops.check_device_status(dev)
+    fla_arm = None
+    if not args.no_fla:
+        def fla_step():
+            from fla.ops.rwkv7 import chunk_rwkv7 as fla_chunk
+            a = -x["kk"]
+            b = (x["kk"].float() * x["a"].float()).to(x["kk"].dtype)
+            fla_chunk(x["r"], x["w"], x["k"], x["v"], a, b, scale=1.0,
+                      initial_state=bank[0, 1:B + 1], output_final_state=True)
+        fla_arm = time_fla(fla_step, args.steps, args.warmup, dev)
+        fla_arm["path"] = "fla.ops.rwkv7.chunk_rwkv7 (Triton), same inputs, state from the bank"
     if rank != 0:
         return None
     step_ms = ms / args.steps
@@ -415,7 +425,27 @@ def run_prefill(args, world, rank, local):
                      "bytes_per_launch": int(byts), "flops_per_launch": int(flops),
                      **tensor_roof(flops, step_ms)},
         "clocks": clk.summary(), "gpu_launches": args.steps,
+        "same_box_fla": fla_arm,
     }
+
+
+def time_fla(fn, steps: int, warmup: int, dev) -> dict:
+    """The same call through flash-linear-attention's own Triton kernel on the
+    same box and inputs (the GPU implementation wkvm runs today), CUDA
+    events; {"unavailable": why} when fla cannot run here."""
+    try:
+        for _ in range(max(warmup, 2)):
+            fn()
+        torch.cuda.synchronize(dev)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(steps):
+            fn()
+        s1.record()
+        torch.cuda.synchronize(dev)
+        return {"ms_per_step": round(s0.elapsed_time(s1) / steps, 4)}
+    except Exception as e:  # fla missing or failing on this box
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
 
 
 def tensor_roof(flops: float, ms: float) -> dict:
@@ -475,6 +505,19 @@ def run_gdn(args, world, rank, local):
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(stop), world, dev)
     ops.check_device_status(dev)
+    fla_arm = None
+    if not args.no_fla:
+        def fla_step():
+            h0 = bank[0, 1:B + 1]
+            if decode:
+                from fla.ops.gated_delta_rule import fused_recurrent_gated_delta_rule as f
+            else:
+                from fla.ops.gated_delta_rule import chunk_gated_delta_rule as f
+            f(x["q"], x["k"], x["v"], x["g"], x["beta"], scale=K ** -0.5, initial_state=h0,
+              output_final_state=True)
+        fla_arm = time_fla(fla_step, args.steps, args.warmup, dev)
+        fla_arm["path"] = (f"fla.ops.gated_delta_rule.{'fused_recurrent' if decode else 'chunk'}"
+                           "_gated_delta_rule (Triton), same inputs, state gathered from the bank")
     if rank != 0:
         return None
     step_ms = ms / args.steps
@@ -510,6 +553,7 @@ def run_gdn(args, world, rank, local):
                    "kernel": kernel},
         "roofline": line_roof, "clocks": clk.summary(),
         "gpu_launches": args.steps * (1 if decode else 2),
+        "same_box_fla": fla_arm,
     }
 
 
@@ -1090,7 +1134,7 @@ def side_workloads(args, world, rank, local):
         torch.cuda.empty_cache()
         out[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "steps",
                                        "warmup", "config", "roofline", "clocks",
-                                       "gpu_launches")}
+                                       "gpu_launches", "same_box_fla")}
     return out
 
 
@@ -1105,6 +1149,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-migration", action="store_true",
                     help="N > 1: leave out the ring migration of parked sessions")
+    ap.add_argument("--no-fla", action="store_true",
+                    help="skip the same-box fla Triton timing of the prefill / GDN workloads")
     ap.add_argument("--no-workloads", action="store_true",
                     help="skip the config 2 / 3 lines the default 1-GPU run adds")
     ap.add_argument("--no-overlap", action="store_true",
