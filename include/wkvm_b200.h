@@ -246,7 +246,11 @@ int wkvm_dplr_prefill_slots(
  * wkvm_gdn_chunk_workspace_bytes) as two launches, a chunk-parallel WY
  * kernel and a sequential state pass; without one as a single kernel (one
  * CTA per sequence, value head and half of V). Other shapes run the
- * recurrent kernel. The workspace is 256-byte aligned or ignored. */
+ * recurrent kernel. The workspace is 256-byte aligned or ignored. The
+ * two-launch path keeps its per-chunk records in fp16 (the tf32
+ * significand) and multiplies in kind::f16; a record value beyond fp16's
+ * range (|v| above ~6e4) is reported as WKVM_ERR_UNSUPPORTED in `status`,
+ * and such inputs run without a workspace (tf32 operands throughout). */
 int wkvm_chunk_gated_delta_rule(
     const void* q, const void* k, const void* v, const void* g,
     const void* beta, void* o,
@@ -272,7 +276,7 @@ int64_t wkvm_gdn_chunk_workspace_bytes(int32_t nseq, int32_t T, int32_t HV, int3
  * for wkvm_chunk_gated_delta_rule without the workspace; K == V == 128 and
  * 16-bit inputs only (WKVM_ERR_SHAPE / WKVM_ERR_DTYPE otherwise). Longer
  * inputs run in windows of chunks; WKVM_ERR_SCRATCH when even one window
- * does not fit (about nseq * HV > 300). Runs on the current device; the
+ * does not fit (about nseq * HV > 480). Runs on the current device; the
  * first call on each device, and the first after a cudaDeviceReset, looks
  * up the array's device address (cudaGetSymbolAddress), so make that first
  * call before any stream capture. All calls share the array: calls that overlap on the GPU (other

@@ -109,3 +109,29 @@ def test_debug_checks_raise_at_the_call(cuda):
     finally:
         ops.set_debug_checks(prev)
     ops.check_device_status(cuda)
+
+
+def test_gdn_prefill_reports_records_beyond_fp16(cuda, monkeypatch):
+    """The two-launch GDN prefill keeps its per-chunk records in fp16. Values
+    too large for fp16 (here |v| ~ 1e5) are reported in the status word as
+    WKVM_ERR_UNSUPPORTED instead of flowing on as infinities; the one-kernel
+    path (no workspace, tf32 operands) handles the same call."""
+    from conftest import REL_TOL, assert_out_close, np32, rel_err
+    from oracle import oracle
+    HV, K, T = 2, 128, 200
+    x = synth.gdn_inputs(1, T, HV, K, seed=6)
+    x["v"] = (x["v"].float() * 1e5).to(torch.bfloat16)
+    d = {k: v.to(cuda) for k, v in x.items()}
+    names = ("q", "k", "v", "g", "beta")
+    ops.check_device_status(cuda)
+    ops.chunk_gated_delta_rule(*(d[n] for n in names), initial_state=d["h0"],
+                               output_final_state=True)
+    with pytest.raises(RuntimeError, match="UNSUPPORTED"):
+        ops.check_device_status(cuda)
+    monkeypatch.setattr(prefill, "GDN_WORKSPACE_LIMIT", 0)
+    o, ht = ops.chunk_gated_delta_rule(*(d[n] for n in names), initial_state=d["h0"],
+                                       output_final_state=True)
+    ops.check_device_status(cuda)
+    ro, rh = oracle.gdn_recurrence(*(np32(x[n]) for n in names), initial_state=np32(x["h0"]))
+    assert_out_close(o, ro)
+    assert rel_err(ht, rh) < REL_TOL

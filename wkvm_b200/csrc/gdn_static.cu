@@ -11,7 +11,7 @@
 // The array is kGdnScratchBytes (64 MiB) on every GPU that loads the library,
 // held until the process exits. Requests are processed in windows of chunks
 // that fit it; one window must hold one chunk record plus the carried state
-// for every (sequence, value head), so nseq * HV is limited to about 300.
+// for every (sequence, value head), so nseq * HV is limited to about 480.
 #include <mutex>
 
 #include "common.cuh"

@@ -61,14 +61,20 @@ __host__ __device__ constexpr uint32_t hoff16(int row, int k, uint32_t sbo) {
          (uint32_t)(k & 7) * 2;
 }
 
-// Eight floats as fp16, one 16-byte store.
-__device__ __forceinline__ void st_h8(uint8_t* p, const float* x) {
+// Eight floats as fp16, one 16-byte store; `mx` keeps the largest magnitude
+// written (a record value beyond fp16's range is reported, not stored silently
+// as infinity).
+__device__ __forceinline__ void st_h8(uint8_t* p, const float* x, float& mx) {
   uint4 u;
   __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+  for (int i = 0; i < 4; ++i) {
+    h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+    mx = fmaxf(mx, fmaxf(fabsf(x[2 * i]), fabsf(x[2 * i + 1])));
+  }
   *reinterpret_cast<uint4*>(p) = u;
 }
+constexpr float kHalfMax = 65504.f;
 static_assert(REC_BYTES % 128 == 0 && PART_B % 16 == 0 && PART_U % 16 == 0,
               "record alignment");
 
@@ -261,6 +267,7 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
   const uint32_t id_gram = tc::idesc_f16(128, 64, kBf16);
   const uint32_t id_s = tc::idesc_tf32(128, 64);
 
+  float rmax = 0.f;  // largest magnitude this thread wrote to an fp16 record
 #pragma unroll 1
   for (int it = 0; j < njobs; ++it, j += gridDim.x) {
     const int st = it & 1;
@@ -371,7 +378,7 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
         }
         tc::tmem_st32(tq + T_AK + s0, x);
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) st_h8(rec + R_KT + hoff16(l, s0 + i, SBOH64), y + i);
+        for (int i = 0; i < 32; i += 8) st_h8(rec + R_KT + hoff16(l, s0 + i, SBOH64), y + i, rmax);
         // Q~ (rows 64..127 of [W; Q~]): piece e -> row t = 8 g + (e & 7), 8
         // columns from (e >> 3) & 15; eight lanes fill 128 contiguous bytes
 #pragma unroll
@@ -384,7 +391,7 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
           float qv[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) qv[i] = to_f32(h[i]) * f;
-          st_h8(rec + R_WQ + hoff16(64 + t, k8, SBOH128), qv);
+          st_h8(rec + R_WQ + hoff16(64 + t, k8, SBOH128), qv, rmax);
         }
         tc::tmem_st_wait();
       }
@@ -422,7 +429,7 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
             x[i] = s <= t ? f * s_rk[s] * __expf(Gt - s_G[s]) * x[i] : 0.f;
           }
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) st_h8(rec + R_AQK + hoff16(t, s0 + i, SBOH64), x + i);
+          for (int i = 0; i < 32; i += 8) st_h8(rec + R_AQK + hoff16(t, s0 + i, SBOH64), x + i, rmax);
         }
       }
       __syncthreads();
@@ -454,7 +461,10 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
         tc::tmem_ld32(tq + T_D1 + t0, x);  // U^T[v = l][t0 + i] -> U[t][v], 128 B per warp and t
         __half* ucol = reinterpret_cast<__half*>(rec + R_U) + (l >> 6) * 64 * 64 + (l & 63);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) ucol[(t0 + i) * 64] = __float2half_rn(x[i]);
+        for (int i = 0; i < 32; ++i) {
+          ucol[(t0 + i) * 64] = __float2half_rn(x[i]);
+          rmax = fmaxf(rmax, fabsf(x[i]));
+        }
         // W^T[k = l][t0 + i] -> row-major W[t][k] in the spent stage (row
         // stride W_ROW: lanes hit distinct banks), copied out below
         tc::tmem_ld32(tq + T_DW + t0, x);
@@ -475,7 +485,7 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
           *reinterpret_cast<float4*>(wv) = *reinterpret_cast<const float4*>(wst + t * W_ROW + k8);
           *reinterpret_cast<float4*>(wv + 4) =
               *reinterpret_cast<const float4*>(wst + t * W_ROW + k8 + 4);
-          st_h8(rec + R_WQ + hoff16(t, k8, SBOH128), wv);
+          st_h8(rec + R_WQ + hoff16(t, k8, SBOH128), wv, rmax);
         }
       }
       // the next job overwrites this stage only after every thread is past here
@@ -488,6 +498,7 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
     for (int i = 0; i < 4; ++i) sc_cur[i] = sc_next[i];
   }
 
+  if (!(rmax <= kHalfMax)) report(p.status, WKVM_ERR_UNSUPPORTED);  // also NaN
   // no TMA load may still target this CTA's shared memory
   for (int st = 0; st < 2; ++st)
     if (((in_pending >> st) & 1u) && warp == 0 &&
