@@ -238,25 +238,37 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
       tma::load_rows(base + ST_V + b * BOX, &maps.v, J.hv, tok, &in_bar[st], 64 * b);
     }
   };
-  // per-token decay and beta of job J into warp 0's registers
-  auto scalars_in = [&](const Job& J, float (&x)[4]) {
-    x[0] = x[1] = x[2] = x[3] = 0.f;
+  // per-token decay and beta of job J into warp 0's registers, as raw bits:
+  // the conversion to fp32 waits for the load, so it happens at the use
+  const bool gf32 = p.gates_f32;
+  auto scalars_in = [&](const Job& J, uint32_t (&x)[4]) {
+    x[0] = x[1] = x[2] = x[3] = 0u;
     if (warp == 0) {
+      const int64_t i0 = (J.tok0 + lane) * HV + J.hv, i1 = (J.tok0 + lane + 32) * HV + J.hv;
+      auto raw = [&](const void* b, int64_t i) -> uint32_t {
+        return gf32 ? static_cast<const uint32_t*>(b)[i]
+                    : (uint32_t) static_cast<const uint16_t*>(b)[i];
+      };
       if (lane < J.clen) {
-        x[0] = load_gate<Tin>(p.g, (J.tok0 + lane) * HV + J.hv, p.gates_f32);
-        x[2] = load_gate<Tin>(p.beta, (J.tok0 + lane) * HV + J.hv, p.gates_f32);
+        x[0] = raw(p.g, i0);
+        x[2] = raw(p.beta, i0);
       }
       if (lane + 32 < J.clen) {
-        x[1] = load_gate<Tin>(p.g, (J.tok0 + lane + 32) * HV + J.hv, p.gates_f32);
-        x[3] = load_gate<Tin>(p.beta, (J.tok0 + lane + 32) * HV + J.hv, p.gates_f32);
+        x[1] = raw(p.g, i1);
+        x[3] = raw(p.beta, i1);
       }
     }
+  };
+  auto gate = [&](uint32_t bits) -> float {
+    if (gf32) return __uint_as_float(bits);
+    const uint16_t h = (uint16_t)bits;
+    return to_f32(*reinterpret_cast<const Tin*>(&h));
   };
 
   int j = blockIdx.x;
   Job cur = job_of(p, j < njobs ? j : 0);
   if (j >= njobs) cur.clen = 0;
-  float sc_cur[4], sc_next[4];
+  uint32_t sc_cur[4], sc_next[4];
   tc::fence_before_sync();
   __syncthreads();  // barriers initialised before the first load
   tc::fence_after_sync();
@@ -302,9 +314,9 @@ gdn_wy_kernel(WyArgs p, int njobs, const __grid_constant__ WyMaps maps) {
         }
       }
       if (warp == 0) {  // inclusive decay scan
-        float a = sc_cur[0], b = sc_cur[1];
-        s_beta[lane] = sc_cur[2];
-        s_beta[lane + 32] = sc_cur[3];
+        float a = gate(sc_cur[0]), b = gate(sc_cur[1]);
+        s_beta[lane] = gate(sc_cur[2]);
+        s_beta[lane + 32] = gate(sc_cur[3]);
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
           const float ua = __shfl_up_sync(0xffffffffu, a, off);
