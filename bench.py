@@ -1083,6 +1083,36 @@ def _cpu_sample(slots: int, threads: int, seed: int = 0):
     return time.perf_counter() - t0
 
 
+def torch_reference_cfg0(steps: int = 16, seed: int = 0) -> dict:
+    """BASELINE config 0 (B=8 slots, L=12, H=12, N=64) through the reference's
+    own PyTorch CPU recurrence, fla's dplr_recurrence
+    (fla/ops/generalized_delta_rule/dplr/naive.py:16), fp32, on the host's
+    cores: `steps` tokens per layer for every layer. fla forces a q * K^-0.5
+    scale there; r is pre-multiplied by sqrt(K) so the work and the result are
+    RWKV-7's scale-1 step."""
+    try:
+        from fla.ops.generalized_delta_rule.dplr.naive import dplr_recurrence
+    except Exception as e:  # fla missing on this host
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:120]}"}
+    from wkvm_b200 import synth
+    B0, L0, H0, N0 = 8, 12, 12, 64
+    hf = lambda t: t.float().transpose(1, 2).contiguous()  # [B, H, T, D]
+    layers = []
+    for layer in range(L0):
+        x = synth.rwkv7_inputs(B0, steps, H0, N0, seed=seed * 100 + layer)
+        layers.append((hf(x["r"]) * N0 ** 0.5, hf(x["k"]), hf(x["v"]), -hf(x["kk"]),
+                       hf(x["kk"]) * hf(x["a"]), hf(x["w"]), x["h0"]))
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        for q, k, v, al, be, w, h0 in layers:
+            dplr_recurrence(q, k, v, al, be, w, initial_state=h0.clone(), output_final_state=True)
+    sec = time.perf_counter() - t0
+    return {"value": round(B0 * steps / sec, 2), "unit": "tokens/s",
+            "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"BASELINE config 0: {B0} slots x {L0} layers x {H0} heads, {steps} tokens, "
+                      "fla's dplr_recurrence (torch, fp32, CPU)"}
+
+
 def cpu_baseline(slots: int):
     threads = os.cpu_count() or 1
     reps, total = 0, 0.0
@@ -1092,7 +1122,8 @@ def cpu_baseline(slots: int):
     return {"value": round(reps * slots / total, 2), "unit": "tokens/s", "cores": threads,
             "kind": "port",
             "sample": f"{reps} x ({slots} slots x 24 layers x 32 heads, one token) through the "
-                      f"fp32 C oracle (oracle/wkv_oracle.c), {threads} threads"}
+                      f"fp32 C oracle (oracle/wkv_oracle.c), {threads} threads",
+            "reference_torch_cfg0": torch_reference_cfg0()}
 
 
 def run_reference(args, world, rank):
@@ -1116,7 +1147,8 @@ def run_reference(args, world, rank):
                    "global_batch": slots, "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{slots} slots x 24 layers x 32 heads per step, fp32 C "
-                                   "restatement of fla's recurrence (oracle/wkv_oracle.c)"},
+                                   "restatement of fla's recurrence (oracle/wkv_oracle.c)",
+                         "reference_torch_cfg0": torch_reference_cfg0()},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
