@@ -1122,8 +1122,7 @@ def cpu_baseline(slots: int):
     return {"value": round(reps * slots / total, 2), "unit": "tokens/s", "cores": threads,
             "kind": "port",
             "sample": f"{reps} x ({slots} slots x 24 layers x 32 heads, one token) through the "
-                      f"fp32 C oracle (oracle/wkv_oracle.c), {threads} threads",
-            "reference_torch_cfg0": torch_reference_cfg0()}
+                      f"fp32 C oracle (oracle/wkv_oracle.c), {threads} threads"}
 
 
 def run_reference(args, world, rank):
