@@ -718,7 +718,7 @@ def run_cfg4(args, world, rank, local):
 
 
 def run_hibernate(args, world, rank, local):
-    """Snapshot tier (SURVEY next-row 3): hibernate 64 sessions of the RWKV-7
+    """Snapshot tier: hibernate 64 sessions of the RWKV-7
     1.5B state shape (12.19 MiB each) from the arena to pinned host memory
     and wake them back, batched (store_io: one kernel per family per batch)
     versus the reference's per-session flow (wkvm/store.py:127-133: strided
