@@ -694,14 +694,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
           tc::mma_commit(&mb_ma);
           pend_m = 1;
         }
-        // the u pass is done: MMA A read this buffer of [W; Q~] and the
-        // workers read U, so chunk i+2's [W; Q~] and chunk i+1's U go out
+        // the u pass is done (MMA A read this buffer of [W; Q~], the
+        // workers read U); MMA B: S^T += u^T K~ ; O^T += u^T A_qk^T, once
+        // K~ / A_qk landed
         if (!(ok = tc::mbar_wait(&mb_w, ph))) break;
         pend_m = 0;  // the workers saw MMA A complete
         tc::fence_after_sync();
-        if (i + 2 < cnt) issue_a(i + 2);
-        if (i + 1 < cnt) issue_u(i + 1);
-        // MMA B: S^T += u^T K~ ; O^T += u^T A_qk^T, once K~ / A_qk landed
         if (!(ok = tc::mbar_wait(&mb_b, ph))) break;
         pend_b = 0;
         {
@@ -718,6 +716,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_kernel(StateArgs p) {
           tc::mma_commit(&mb_mb);
           pend_m = 1;
         }
+        // while MMA B runs: chunk i+2's [W; Q~] into the buffer MMA A read,
+        // chunk i+1's U into the one the u pass read
+        if (i + 2 < cnt) issue_a(i + 2);
+        if (i + 1 < cnt) issue_u(i + 1);
         // the workers saw MMA B complete and refreshed the fp16 S^T
         if (!(ok = tc::mbar_wait(&mb_c, ph))) break;
         pend_m = 0;
