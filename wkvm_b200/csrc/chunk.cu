@@ -574,7 +574,11 @@ dplr_chunk_kernel(ChunkArgs p, const __grid_constant__ InMaps maps) {
         if (t < clen) store_row(go + ((tok0 + t) * H + hh) * HD + c0, x);
       }
     }
-    sync_tc();
+    // the next chunk's first barrier (its TMA wait) orders these TMEM reads
+    // and S^T writes before anything that touches them again: T_D3 is next
+    // written by MMA S and S^T next read by MMA 4, each behind a fenced
+    // barrier of its own
+    tc::fence_before_sync();
   }
 
   // no TMA load may still target this CTA's shared memory
